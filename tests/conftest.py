@@ -1,0 +1,11 @@
+import pathlib
+import sys
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU and the built CUDA library")
+    config.addinivalue_line("markers", "slow: true Wan shapes (set WAN_FLASH_SLOW_TESTS=1)")

@@ -1,0 +1,275 @@
+// C ABI of the Wan attention hot path (declared in include/wan_flash.h).
+//
+// Host side of each launch: argument checks, TMA tensor-map encoding
+// (driver entry point fetched through the runtime, so the library has no
+// link-time dependency on libcuda), one-time per-device kernel attributes,
+// and the launch on the caller's stream.  Nothing here allocates device
+// memory: every buffer is the caller's.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "wan_flash.h"
+#include "wf_common.cuh"
+#include "wf_kernels.h"
+
+namespace wf {
+
+namespace {
+
+thread_local char t_last_error[512] = {0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(WF_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::mutex g_mu;
+EncodeTiledFn g_encode = nullptr;
+constexpr int kMaxDevices = 64;
+bool g_dev_ready[kMaxDevices] = {false};
+int g_dev_sms[kMaxDevices] = {0};
+
+int get_encode(EncodeTiledFn* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      return fail(WF_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable (%s)", cudaGetErrorName(e));
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  *out = g_encode;
+  return WF_OK;
+}
+
+// Per-device one-time set-up: verify sm_100, record the SM count, opt the
+// big kernels into their dynamic shared memory.
+int device_setup(int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(WF_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+  *dev_out = dev;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_dev_ready[dev]) return WF_OK;
+  int major = 0, minor = 0, sms = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (major != 10 || minor != 0)
+    return fail(WF_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major, minor);
+  e = cudaFuncSetAttribute(wf_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd smem)");
+  e = cudaFuncSetAttribute(wf_bwd_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem_bytes());
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd smem)");
+  g_dev_sms[dev] = sms;
+  g_dev_ready[dev] = true;
+  return WF_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 4-D map over a contiguous (b, s, h, 128) bf16 tensor: dims {d, s, h, b},
+// box {64, 128, 1, 1} with the 128-byte swizzle (one 128-row x 128-byte box).
+int make_bshd_map(CUtensorMap* map, const void* ptr, int b, int s, int h) {
+  EncodeTiledFn enc;
+  int rc = get_encode(&enc);
+  if (rc) return rc;
+  const cuuint64_t dims[4] = {128, (cuuint64_t)s, (cuuint64_t)h, (cuuint64_t)b};
+  const cuuint64_t strides[3] = {(cuuint64_t)h * 256, 256, (cuuint64_t)s * h * 256};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for (%d,%d,%d,128)", (int)r, b, s, h);
+  return WF_OK;
+}
+
+int check_dims(int b, int s1, int s2, int h) {
+  if (b < 0 || s1 < 0 || s2 < 0 || h < 0) return fail(WF_ERR_INVALID_ARG, "negative size");
+  if (h > 65535 || b > 65535) return fail(WF_ERR_UNSUPPORTED, "h=%d / b=%d exceed the grid limits", h, b);
+  // TMA coordinates and strides: s*h*256 must stay below 2^40
+  if ((double)s1 * h * 256.0 >= 1099511627776.0 || (double)s2 * h * 256.0 >= 1099511627776.0)
+    return fail(WF_ERR_UNSUPPORTED, "sequence too long for a TMA stride");
+  return WF_OK;
+}
+
+int launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return WF_OK;
+}
+
+}  // namespace
+}  // namespace wf
+
+using namespace wf;
+
+extern "C" {
+
+int wf_version(void) { return 100; }
+
+int wf_last_error(char* buf, int len) {
+  if (!buf || len <= 0) return WF_ERR_INVALID_ARG;
+  snprintf(buf, (size_t)len, "%s", t_last_error);
+  return WF_OK;
+}
+
+int wf_num_sms(void) {
+  int dev = 0;
+  if (device_setup(&dev)) return 0;
+  return g_dev_sms[dev];
+}
+
+int wf_set_wait_limit_ns(unsigned long long ns) {
+  if (ns == 0) return fail(WF_ERR_INVALID_ARG, "wait limit must be > 0");
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(wait limit)");
+  return WF_OK;
+}
+
+int wf_device_status(unsigned int* info) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned int code = 0, inf[4] = {0, 0, 0, 0};
+  e = cudaMemcpyFromSymbol(&code, g_err_code, sizeof(code));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(err)");
+  e = cudaMemcpyFromSymbol(inf, g_err_info, sizeof(inf));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(info)");
+  if (info) memcpy(info, inf, sizeof(inf));
+  if (code != 0) {
+    const unsigned int zero[5] = {0, 0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_err_code, zero, sizeof(unsigned int));
+    cudaMemcpyToSymbol(g_err_info, zero + 1, sizeof(inf));
+    return fail((int)code, "device error %d: block (%u,%u,%u) role %u tag %u", (int)code, inf[0] & 0xFFFF,
+                inf[0] >> 16, inf[1], inf[2], inf[3]);
+  }
+  return WF_OK;
+}
+
+int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int b, int sq, int skv, int h,
+           const wf_fwd_cfg* cfg, void* stream) {
+  int rc = check_dims(b, sq, skv, h);
+  if (rc) return rc;
+  if (b == 0 || sq == 0 || h == 0) return WF_OK;
+  if (skv == 0) return fail(WF_ERR_UNSUPPORTED, "skv == 0: attention over an empty key set");
+  if (!q || !k || !v || !o || !lse) return fail(WF_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (reinterpret_cast<uintptr_t>(lse) & 3))
+    return fail(WF_ERR_MISALIGNED, "q/k/v/o must be 16-byte aligned and lse 4-byte aligned");
+  int dev;
+  if ((rc = device_setup(&dev))) return rc;
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_bshd_map(&mq, q, b, sq, h)) || (rc = make_bshd_map(&mk, k, b, skv, h)) ||
+      (rc = make_bshd_map(&mv, v, b, skv, h)))
+    return rc;
+  FwdParams p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.lse = lse;
+  p.sq = sq;
+  p.skv = skv;
+  p.h = h;
+  p.n_blocks = (skv + 127) / 128;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  p.rescale_threshold = cfg ? cfg->rescale_threshold : 8.0f;
+  dim3 grid((sq + 255) / 256, h, b);
+  wf_fwd_kernel<<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, p);
+  return launch_check("wf_fwd launch");
+}
+
+int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* lse_log2, float* dq_accum, int b,
+               int sq, int sq_rounded, int h, void* stream) {
+  int rc = check_dims(b, sq, sq_rounded, h);
+  if (rc) return rc;
+  if (sq_rounded != (sq + 127) / 128 * 128) return fail(WF_ERR_INVALID_ARG, "sq_rounded must be ceil(sq/128)*128");
+  if (b == 0 || sq == 0 || h == 0) return WF_OK;
+  if (!o || !dO || !lse || !dpsum || !lse_log2 || !dq_accum) return fail(WF_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(o) || !aligned16(dO) || !aligned16(dpsum) || !aligned16(lse_log2) || !aligned16(dq_accum))
+    return fail(WF_ERR_MISALIGNED, "o/dO/dpsum/lse_log2/dq_accum must be 16-byte aligned");
+  int dev;
+  if ((rc = device_setup(&dev))) return rc;
+  dim3 grid(sq_rounded / 64, h, b);
+  wf_bwd_pre_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(dO), lse, dpsum, lse_log2,
+      dq_accum, sq, sq_rounded, h);
+  return launch_check("wf_bwd_pre launch");
+}
+
+int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, const float* lse_log2,
+                const float* dpsum, float* dq_accum, void* dk, void* dv, int b, int sq, int skv, int h,
+                const wf_bwd_cfg* cfg, void* stream) {
+  int rc = check_dims(b, sq, skv, h);
+  if (rc) return rc;
+  if (b == 0 || h == 0 || skv == 0) return WF_OK;
+  if (sq == 0) return fail(WF_ERR_UNSUPPORTED, "sq == 0: the caller must zero dk/dv");
+  if (!q || !k || !v || !dO || !lse_log2 || !dpsum || !dq_accum || !dk || !dv)
+    return fail(WF_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dO) || !aligned16(lse_log2) ||
+      !aligned16(dpsum) || !aligned16(dq_accum) || !aligned16(dk) || !aligned16(dv))
+    return fail(WF_ERR_MISALIGNED, "all buffers must be 16-byte aligned");
+  const int nsplit = cfg ? cfg->nsplit : 1;
+  int dev;
+  if ((rc = device_setup(&dev))) return rc;
+  BwdParams p;
+  p.lse_log2 = lse_log2;
+  p.dpsum = dpsum;
+  p.dq_accum = dq_accum;
+  p.dk = dk;
+  p.dv = dv;
+  p.sq = sq;
+  p.skv = skv;
+  p.h = h;
+  p.m_blocks = (sq + 127) / 128;
+  p.sq_rounded = p.m_blocks * 128;
+  p.n_blocks = (skv + 127) / 128;
+  p.skv_rounded = p.n_blocks * 128;
+  if (nsplit < 1 || nsplit > p.m_blocks) return fail(WF_ERR_INVALID_ARG, "nsplit=%d outside [1, %d]", nsplit, p.m_blocks);
+  p.m_chunk = (p.m_blocks + nsplit - 1) / nsplit;
+  p.accum_dkv = nsplit > 1 ? 1 : 0;
+  p.scale = (float)(1.0 / std::sqrt(128.0));
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  CUtensorMap mq, mk, mv, mdo;
+  if ((rc = make_bshd_map(&mq, q, b, sq, h)) || (rc = make_bshd_map(&mk, k, b, skv, h)) ||
+      (rc = make_bshd_map(&mv, v, b, skv, h)) || (rc = make_bshd_map(&mdo, dO, b, sq, h)))
+    return rc;
+  const int splits = (p.m_blocks + p.m_chunk - 1) / p.m_chunk;  // every split owns >= 1 m-block
+  dim3 grid(p.n_blocks * splits, h, b);
+  wf_bwd_main_kernel<<<grid, kBwdThreads, bwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mdo,
+                                                                                                       p);
+  return launch_check("wf_bwd_main launch");
+}
+
+int wf_bwd_convert(const float* accum, void* out, float scale, int b, int s, int h, void* stream) {
+  int rc = check_dims(b, s, s, h);
+  if (rc) return rc;
+  if (b == 0 || s == 0 || h == 0) return WF_OK;
+  if (!accum || !out) return fail(WF_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(accum) || !aligned16(out)) return fail(WF_ERR_MISALIGNED, "accum/out must be 16-byte aligned");
+  int dev;
+  if ((rc = device_setup(&dev))) return rc;
+  const int s_rounded = (s + 127) / 128 * 128;
+  dim3 grid(s_rounded / 32, h, b);
+  wf_convert_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      accum, reinterpret_cast<__nv_bfloat16*>(out), scale, s, s_rounded, h);
+  return launch_check("wf_bwd_convert launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,53 @@
+// Kernel parameter blocks and launch-side declarations shared by the kernel
+// translation units and the C ABI (wf_capi.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace wf {
+
+struct FwdParams {
+  __nv_bfloat16* o;
+  float* lse;
+  int sq, skv, h;
+  int n_blocks;            // ceil(skv / 128)
+  float scale_log2;        // log2(e) / sqrt(128)
+  float rescale_threshold; // log2 units
+};
+
+struct BwdParams {
+  const float* lse_log2;   // (b, h, sq_rounded)
+  const float* dpsum;      // (b, h, sq_rounded)
+  float* dq_accum;         // tiled, b*h*sq_rounded*128
+  void* dk;                // bf16 (b, skv, h, 128) or fp32 tiled accumulator
+  void* dv;
+  int sq, skv, h;
+  int sq_rounded, m_blocks, n_blocks, skv_rounded;
+  int accum_dkv;           // 1: dk/dv are fp32 tiled accumulators (split-M)
+  int m_chunk;             // split-M: m-blocks per CTA
+  float scale;             // 1/sqrt(128)
+  float scale_log2;        // log2(e)/sqrt(128)
+};
+
+__global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, FwdParams p);
+__global__ void wf_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                                   BwdParams p);
+__global__ void wf_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
+                                  const float* __restrict__ lse, float* __restrict__ dpsum,
+                                  float* __restrict__ lse_log2, float* __restrict__ dq_accum, int sq,
+                                  int sq_rounded, int h);
+__global__ void wf_convert_kernel(const float* __restrict__ accum, __nv_bfloat16* __restrict__ out, float scale,
+                                  int s, int s_rounded, int h);
+
+size_t fwd_smem_bytes();
+size_t bwd_smem_bytes();
+
+constexpr int kFwdThreads = 320;
+constexpr int kBwdThreads = 320;
+
+}  // namespace wf

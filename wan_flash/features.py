@@ -1,0 +1,113 @@
+"""Feature-flag registry (same accessors as the reference's
+``wan_flash/features.py:28-100``: ``get``, ``get_bwd``, ``set_overrides``,
+``set_bwd_overrides``, ``reset``), with the B200 kernels' options.
+
+Forward flags
+  rescale_skip_threshold  skip the O rescale while the running row max grew by
+                          at most this many log2 units (exact by max-shift
+                          invariance; only rounding differs).  0.0 = always
+                          rescale.
+  scheduler               "auto" | "single" | "persistent".  This build has the
+                          one-CTA-per-tile grid; "persistent" is accepted and
+                          currently launches the same grid.
+  tile_m / tile_n         fixed at 128 x 128 (two 128-row query tiles per CTA).
+  num_stages              K/V ring depth in (K, V) pairs (fixed at 2).
+  cluster_mn              (1, 1) only: no TMA multicast anywhere (multi-GPU
+                          runs must never issue multicast loads on this pool).
+  intra_wg_overlap        the two query tiles of a CTA ping-pong softmax and
+                          tensor work (always on in this design).
+  mma_pv_is_rs            P feeds the PV MMA from tensor memory (always on).
+
+Backward flags
+  tile_m / tile_n         fixed at 128 x 128.
+  num_stages              Q/dO double buffering (fixed at 2).
+  nsplit                  split-M factor; 0 = auto (1 when the
+                          (n_blocks*h*b) grid fills the GPU, otherwise the
+                          smallest split with >= 95% wave efficiency).  With
+                          nsplit > 1 dK/dV go through fp32 reductions and a
+                          convert, which makes them nondeterministic.
+  cluster_n               1 only (no multicast).
+"""
+
+from dataclasses import dataclass, replace
+
+
+@dataclass(frozen=True)
+class FwdFeatures:
+    rescale_skip_threshold: float = 8.0
+    intra_wg_overlap: bool = True
+    mma_pv_is_rs: bool = True
+    num_stages: int = 2
+    tile_m: int = 128
+    tile_n: int = 128
+    scheduler: str = "auto"
+    cluster_mn: tuple = (1, 1)
+
+
+@dataclass(frozen=True)
+class BwdFeatures:
+    tile_m: int = 128
+    tile_n: int = 128
+    num_stages: int = 2
+    nsplit: int = 0
+    cluster_n: int = 1
+
+
+_current = FwdFeatures()
+_current_bwd = BwdFeatures()
+
+
+def _validate_fwd(f: FwdFeatures):
+    if f.tile_m != 128 or f.tile_n != 128:
+        raise ValueError("the sm_100a forward is built for 128x128 tiles")
+    if f.num_stages != 2:
+        raise ValueError("the forward K/V ring holds 2 (K, V) pairs")
+    if tuple(f.cluster_mn) != (1, 1):
+        raise ValueError("cluster_mn must be (1, 1): this build issues no multicast TMA loads")
+    if f.scheduler not in ("auto", "single", "persistent"):
+        raise ValueError(f"unknown scheduler {f.scheduler!r}")
+    if not (f.rescale_skip_threshold >= 0.0):
+        raise ValueError("rescale_skip_threshold must be >= 0")
+    if not f.intra_wg_overlap or not f.mma_pv_is_rs:
+        raise ValueError("intra_wg_overlap and mma_pv_is_rs are structural in this design")
+
+
+def _validate_bwd(f: BwdFeatures):
+    if f.tile_m != 128 or f.tile_n != 128:
+        raise ValueError("the sm_100a backward is built for 128x128 tiles")
+    if f.num_stages != 2:
+        raise ValueError("the backward double-buffers Q/dO (num_stages=2)")
+    if f.nsplit < 0:
+        raise ValueError("nsplit must be >= 0 (0 = auto)")
+    if f.cluster_n != 1:
+        raise ValueError("cluster_n must be 1: this build issues no multicast TMA loads")
+
+
+def get() -> FwdFeatures:
+    return _current
+
+
+def get_bwd() -> BwdFeatures:
+    return _current_bwd
+
+
+def set_overrides(**kw):
+    global _current
+    new = replace(_current, **kw)
+    _validate_fwd(new)
+    _current = new
+    return _current
+
+
+def set_bwd_overrides(**kw):
+    global _current_bwd
+    new = replace(_current_bwd, **kw)
+    _validate_bwd(new)
+    _current_bwd = new
+    return _current_bwd
+
+
+def reset():
+    global _current, _current_bwd
+    _current = FwdFeatures()
+    _current_bwd = BwdFeatures()

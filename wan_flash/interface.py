@@ -1,0 +1,200 @@
+"""Host driver: torch tensors -> the sm_100a C ABI (libwanflash.so).
+
+Same API and contract as the reference driver (``wan_flash/interface.py`` of
+Quarky93/wan-flash):
+
+wan_flash_fwd(q, k, v) -> (o, lse)                      (interface.py:33-75)
+  q: (b, s_q, h, d) bf16, k/v: (b, s_kv, h, d) bf16
+  o: (b, s_q, h, d) bf16, lse: (b, h, s_q) fp32, NATURAL log.
+
+wan_flash_bwd(q, k, v, o, lse, do) -> (dq, dk, dv)      (interface.py:98-196)
+  lse: natural log, (b, h, s_q) fp32.  dq is accumulated with fp32
+  reductions, so it is nondeterministic (as in the reference).
+
+wan_flash_attn(q, k, v) -> o                            (interface.py:199-215)
+  autograd.Function chaining the two.
+
+Contract violations raise AssertionError (the reference uses ``assert``);
+non-contiguous inputs are made contiguous.  Outputs and workspaces are torch
+allocations made here; the kernels run on ``torch.cuda.current_stream()``
+and nothing synchronises.  There is no CPU path: the CUDA library must be
+built (``python -m wan_flash.build``) and the tensors must live on an
+sm_100 GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from wan_flash import _lib, features
+from wan_flash.shapes import BWD_TILE_M, TILE_N, sm_count
+
+_SM_CACHE: dict = {}
+
+
+def _sms(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_CACHE:
+        _SM_CACHE[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_CACHE[idx]
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t if t.is_contiguous() else t.contiguous()
+    if t.data_ptr() % 16 != 0:  # a contiguous view with an odd storage offset
+        t = t.clone()
+    return t
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def wan_flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    assert q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+    assert q.dim() == 4 and k.dim() == 4 and v.dim() == 4
+    b, sq, h, d = q.shape
+    bk, skv, hk, dk = k.shape
+    assert (b, h, d) == (bk, hk, dk) and v.shape == k.shape
+    assert d == 128, "specialized for head_dim=128"
+    assert q.is_cuda and k.device == q.device and v.device == q.device, "tensors must be on one CUDA device"
+    assert skv > 0 or sq == 0 or b == 0 or h == 0, "attention over an empty key set"
+    q, k, v = (_aligned(t) for t in (q, k, v))
+
+    o = torch.empty_like(q)
+    lse = torch.empty(b, h, sq, device=q.device, dtype=torch.float32)
+    if o.numel() == 0:
+        return o, lse
+
+    f = features.get()
+    cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler], 0)
+    with torch.cuda.device(q.device):
+        rc = _lib.lib().wf_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), b, sq, skv, h,
+                               ctypes.byref(cfg), ctypes.c_void_p(_stream_ptr(q.device)))
+    _lib.check(rc)
+    return o, lse
+
+
+def _auto_nsplit(base_ctas: int, m_blocks: int, sm_count: int = 148) -> int:
+    """Split-M factor for the backward main kernel (reference: interface.py:78-95).
+
+    1 when the (n_blocks*h*b) grid fills the GPU well; otherwise the smallest
+    split with >= 95% wave efficiency (filling partial waves).  The SM count
+    is the device's (148 on B200), not the reference's hard-coded 132.
+    """
+
+    def eff(ctas):
+        return ctas / (sm_count * -(-ctas // sm_count))
+
+    if eff(base_ctas) >= 0.85:
+        return 1
+    best_k, best_eff = 1, 0.0
+    for cand in range(1, min(m_blocks, 64) + 1):
+        e = eff(base_ctas * cand)
+        if base_ctas * cand >= sm_count and e >= 0.95:
+            return cand
+        if e > best_eff:
+            best_k, best_eff = cand, e
+    return best_k
+
+
+def bwd_plan(b: int, sq: int, skv: int, h: int, sms: int | None = None) -> dict:
+    """Tile / split arithmetic of one backward call (host logic, no device)."""
+    f = features.get_bwd()
+    sq_rounded = -(-sq // BWD_TILE_M) * BWD_TILE_M
+    m_blocks = sq_rounded // BWD_TILE_M
+    n_blocks = -(-skv // TILE_N)
+    skv_rounded = n_blocks * TILE_N
+    sms = sms if sms is not None else sm_count()
+    nsplit = f.nsplit if f.nsplit > 0 else _auto_nsplit(n_blocks * h * b, m_blocks, sms)
+    nsplit = max(1, min(nsplit, m_blocks))
+    return {
+        "sq_rounded": sq_rounded, "m_blocks": m_blocks, "n_blocks": n_blocks,
+        "skv_rounded": skv_rounded, "nsplit": nsplit,
+    }
+
+
+def wan_flash_bwd(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    o: torch.Tensor,
+    lse: torch.Tensor,
+    do: torch.Tensor,
+):
+    """(b,s,h,d) bf16 q/k/v/o/do; lse (b,h,s_q) fp32 natural log ->
+    (dq, dk, dv) bf16 (b,s,h,d)."""
+    assert all(t.dtype == torch.bfloat16 for t in (q, k, v, o, do))
+    assert lse.dtype == torch.float32
+    b, sq, h, d = q.shape
+    bk, skv, hk, dk_ = k.shape
+    assert (b, h, d) == (bk, hk, dk_) and v.shape == k.shape
+    assert o.shape == q.shape and do.shape == q.shape
+    assert lse.shape == (b, h, sq)
+    assert d == 128, "specialized for head_dim=128"
+    assert all(t.is_cuda and t.device == q.device for t in (k, v, o, lse, do)), "tensors must be on one CUDA device"
+    q, k, v, o, do = (_aligned(t) for t in (q, k, v, o, do))
+    lse = lse if lse.is_contiguous() else lse.contiguous()
+
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    if b == 0 or h == 0 or skv == 0:
+        return dq.zero_(), dk, dv
+    if sq == 0:
+        return dq, dk.zero_(), dv.zero_()
+
+    plan = bwd_plan(b, sq, skv, h, _sms(q.device))
+    sq_rounded, nsplit = plan["sq_rounded"], plan["nsplit"]
+    dev = q.device
+    dpsum = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
+    lse_log2 = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
+    dq_accum = torch.empty(b, h, sq_rounded * d, device=dev, dtype=torch.float32)
+    if nsplit > 1:
+        # split-M: dK/dV accumulate in fp32 (must start zeroed)
+        dk_accum = torch.zeros(b, h, plan["skv_rounded"] * d, device=dev, dtype=torch.float32)
+        dv_accum = torch.zeros_like(dk_accum)
+        main_dk, main_dv = dk_accum, dv_accum
+    else:
+        main_dk, main_dv = dk, dv
+
+    L = _lib.lib()
+    stream = ctypes.c_void_p(_stream_ptr(dev))
+    cfg = _lib.BwdCfg(nsplit)
+    with torch.cuda.device(dev):
+        _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(lse_log2), _ptr(dq_accum),
+                                b, sq, sq_rounded, h, stream))
+        _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse_log2), _ptr(dpsum),
+                                 _ptr(dq_accum), _ptr(main_dk), _ptr(main_dv), b, sq, skv, h,
+                                 ctypes.byref(cfg), stream))
+        _lib.check(L.wf_bwd_convert(_ptr(dq_accum), _ptr(dq), ctypes.c_float(1.0 / math.sqrt(d)), b, sq, h, stream))
+        if nsplit > 1:
+            _lib.check(L.wf_bwd_convert(_ptr(dk_accum), _ptr(dk), ctypes.c_float(1.0), b, skv, h, stream))
+            _lib.check(L.wf_bwd_convert(_ptr(dv_accum), _ptr(dv), ctypes.c_float(1.0), b, skv, h, stream))
+    return dq, dk, dv
+
+
+class _WanFlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v):
+        o, lse = wan_flash_fwd(q, k, v)
+        ctx.save_for_backward(q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = wan_flash_bwd(q, k, v, o, lse, do)
+        return dq, dk, dv
+
+
+def wan_flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    """Differentiable attention: our fwd + our bwd. Returns o (b,s,h,d) bf16."""
+    return _WanFlashAttnFn.apply(q, k, v)
