@@ -1,0 +1,408 @@
+"""Benchmark of the Wan attention hot path (forward + backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c3i2v|c4]
+                    [--impl ours|reference]
+
+One step = wan_flash_fwd + wan_flash_bwd over one batch of synthetic bf16
+inputs of the configured Wan shape (default C2: Wan2.1-1.3B 480p
+self-attention, b=1, s=32760, h=12, d=128, q/k/v/dO ~ N(0,1), seed 1).
+TFLOP/s counts 4*b*h*sq*skv*128 for the forward and 2.5x that for the
+backward (the reference's convention, bench/bench.py:89-93).
+
+Multi-GPU (torchrun, one rank per GPU): the work shards by heads with no
+data-path collective.  C2 runs as weak scaling (every rank owns 12 heads of a
+12*N-head problem); C4 (Wan2.1-14B 720p, 40 heads) runs as strong scaling
+(40/N heads per rank).  Time is the max over ranks of CUDA-event time.
+
+Printed (rank 0): one JSON line with value (whole-job TFLOP/s, inputs
+resident in HBM), e2e (same metric through the public API with the inputs
+copied from pinned host memory and o/dq/dk/dv copied back inside the timed
+region), the roofline of the dominant kernel, a CPU baseline (the oracle
+port on the host cores, bounded sample), clocks sampled during the timed
+region, and the number of our kernel launches.
+
+``--impl reference`` times the reference's algorithm on the host cores: the
+reference ships no CPU implementation other than its chunked-fp32 torch
+oracle (tests/oracle.py), so this arm runs the numpy port of that oracle
+(oracle/oracle.py) with all host threads on a bounded sample of the same
+workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: (kind, b, sq, skv, h_total, seed, description)
+    "c2": ("self", 1, 32760, 32760, 12, 1, "Wan2.1-1.3B 480p self-attention fwd+bwd (b=1, s=32760, h=12, d=128)"),
+    "c3": ("cross", 1, 75600, 512, 12, 2, "Wan2.1 cross-attention fwd+bwd (sq=75600, skv=512, h=12)"),
+    "c3i2v": ("cross", 1, 75600, 257, 12, 2, "Wan2.1 I2V image cross-attention fwd+bwd (sq=75600, skv=257, h=12)"),
+    "c4": ("self", 1, 75600, 75600, 40, 3, "Wan2.1-14B 720p self-attention fwd+bwd, head-sharded (b=1, s=75600, h=40)"),
+}
+METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/4/8-GPU"
+NOMINAL_BF16_TFLOPS = 2250.0
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d.get("bf16_tflops_sustained"),
+                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def flops(b, h, sq, skv):
+    f = 4.0 * b * h * sq * skv * 128
+    return f, 2.5 * f
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        try:
+            for line in pathlib.Path(self.path).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        loaded = [x for x in sm if x > 0.5 * max(sm)] if sm else []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- CPU arm
+def _cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        return int(max([i.get("num_threads", 1) for i in threadpool_info()] + [1]))
+    except Exception:
+        return 1
+
+
+class CpuSampler:
+    """The oracle port (fp32 numpy, oracle/oracle.py) on a bounded sample of
+    the workload: head 0, ``rows`` query rows against the full K/V, forward +
+    analytic backward.  Cost is linear in query rows and heads, so TFLOP/s
+    over the sample is the workload's rate on these cores."""
+
+    def __init__(self, cfg_name: str):
+        import numpy as np
+
+        from oracle.oracle import round_bf16
+
+        self.kind, self.b, self.sq, self.skv, self.h, seed, _ = CONFIGS[cfg_name]
+        self.rng = np.random.default_rng(seed)
+        self.k = round_bf16(self.rng.standard_normal((1, 1, self.skv, 128), dtype=np.float32))
+        self.v = round_bf16(self.rng.standard_normal((1, 1, self.skv, 128), dtype=np.float32))
+
+    def run(self, rows: int) -> float:
+        from oracle.oracle import oracle_bwd, oracle_fwd, round_bf16
+
+        import numpy as np
+
+        q = round_bf16(self.rng.standard_normal((1, 1, rows, 128), dtype=np.float32))
+        do = round_bf16(self.rng.standard_normal((1, 1, rows, 128), dtype=np.float32))
+        t0 = time.perf_counter()
+        o, lse = oracle_fwd(q, self.k, self.v)
+        oracle_bwd(q, self.k, self.v, o, lse, do)
+        return time.perf_counter() - t0
+
+    def rows_for(self, seconds: float) -> int:
+        dt = self.run(256)
+        rows = int(256 * seconds / max(dt, 1e-4))
+        return max(256, min(self.sq, rows))
+
+    def flops(self, rows: int) -> float:
+        f, fb = flops(1, 1, rows, self.skv)
+        return f + fb
+
+
+def cpu_sample(cfg_name: str, target_s: float = 12.0):
+    s = CpuSampler(cfg_name)
+    rows = s.rows_for(target_s)
+    dt = s.run(rows)
+    return {
+        "value": s.flops(rows) / dt / 1e12,
+        "unit": "TFLOP/s",
+        "cores": _cpu_threads(),
+        "kind": "port",
+        "sample": (f"oracle/oracle.py fp32 fwd+bwd on head 0: {rows} of {s.sq} query rows x {s.skv} keys "
+                   f"({dt:.1f} s); cost is linear in rows and heads"),
+    }
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=0, help="override heads per GPU (small profiling cases)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    kind, b, sq, skv, h_total, seed, desc = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        # rank 0 alone runs the CPU reference arm; other ranks exit without work
+        if rank == 0:
+            sampler = CpuSampler(args.config)
+            per_step_s = min(20.0, max(1.0, 150.0 / (args.steps + args.warmup)))
+            rows = sampler.rows_for(per_step_s)
+            for _ in range(args.warmup):
+                sampler.run(rows)
+            t = sum(sampler.run(rows) for _ in range(args.steps))
+            value = sampler.flops(rows) * args.steps / t / 1e12
+            cpu = {"value": value, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port",
+                   "sample": (f"per step: oracle/oracle.py fp32 fwd+bwd on head 0, {rows} of {sq} query rows x "
+                              f"{skv} keys; cost is linear in rows and heads")}
+            line = {
+                "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True,
+                "scaling": "weak" if args.config != "c4" else "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded)",
+                "config": {"workload": desc, "global_batch": b, "seq_len": sq, "kv_len": skv,
+                           "heads": h_total, "parallelism": "host cores"},
+                "cpu_baseline": cpu,
+                "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            }
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from wan_flash import _lib, interface
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    if args.config == "c4":
+        assert h_total % world == 0, "40 heads must split evenly over the ranks"
+        h = h_total // world
+        scaling = "strong"
+        global_h = h_total
+    else:
+        h = h_total
+        scaling = "weak"
+        global_h = h_total * world
+    if args.heads > 0:
+        h = args.heads
+        global_h = h * world
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed * 1000 + rank)
+
+    def rnd(s):
+        return torch.randn(b, s, h, 128, device=dev, dtype=torch.float32, generator=gen).to(torch.bfloat16)
+
+    q, k, v, do = rnd(sq), rnd(skv), rnd(skv), rnd(sq)
+    f_fwd, f_bwd = flops(b, h, sq, skv)
+    step_flops = f_fwd + f_bwd
+
+    def step(marks=None):
+        o, lse = interface._fwd_impl(q, k, v, marks)
+        dq, dk, dv = interface._bwd_impl(q, k, v, o, lse, do, marks)
+        return o, dq, dk, dv
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    _lib.check_device()
+    barrier()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    # ---- timed region: K steps, inputs resident in HBM (working set >> L2)
+    all_marks = []
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        marks = []
+        step(marks)
+        all_marks.append(marks)
+    t_end.record()
+    barrier()
+    ms = t_start.elapsed_time(t_end)
+    ms = max_over_ranks(ms)
+    ms_per_step = ms / args.steps
+
+    # per-kernel averages from the marks of the timed region
+    per = {}
+    for marks in all_marks:
+        for (name, ev), (_, ev_next) in zip(marks[:-1], marks[1:]):
+            if name == "end":
+                continue
+            per.setdefault(name, []).append(ev.elapsed_time(ev_next))
+    kern_ms = {n: sum(x) / len(x) for n, x in per.items()}
+
+    # ---- e2e: public API, host (pinned) inputs copied in and results copied out each step
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
+        outs = [torch.empty(t.shape, dtype=torch.bfloat16, pin_memory=True) for t in (q, q, k, v)]
+        from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+
+        def e2e_step():
+            dq_, dk_, dv_ = None, None, None
+            qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, hdo))
+            o_, lse_ = wan_flash_fwd(qd, kd, vd)
+            dq_, dk_, dv_ = wan_flash_bwd(qd, kd, vd, o_, lse_, dod)
+            for dst, src in zip(outs, (o_, dq_, dk_, dv_)):
+                dst.copy_(src, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        barrier()
+        e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+        d2h = sum(t.numel() * t.element_size() for t in outs)
+        e2e = {"value": step_flops * world / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    clk = clocks.stop()
+    _lib.check_device()
+
+    if rank == 0:
+        peaks = load_peaks()
+        value = step_flops * world / (ms_per_step * 1e-3) / 1e12
+        fwd_tf = f_fwd / (kern_ms["fwd"] * 1e-3) / 1e12
+        bwd_chain_ms = sum(kern_ms.get(n, 0.0) for n in ("bwd_pre", "bwd_main", "bwd_convert"))
+        bwd_tf = f_bwd / (bwd_chain_ms * 1e-3) / 1e12
+        main_tf = f_bwd / (kern_ms["bwd_main"] * 1e-3) / 1e12
+        dominant = "bwd_main" if kern_ms["bwd_main"] >= kern_ms["fwd"] else "fwd"
+        dom_flops = f_bwd if dominant == "bwd_main" else f_fwd
+        dom_ms = kern_ms[dominant]
+        achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+        plan = interface.bwd_plan(b, sq, skv, h, torch.cuda.get_device_properties(dev).multi_processor_count)
+        launches_per_step = 1 + 3 + (2 if plan["nsplit"] > 1 else 0)
+        cpu = None
+        if not args.no_cpu and world == 1:
+            cpu = cpu_sample(args.config)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": scaling,
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16; no dataset)",
+            "config": {
+                "workload": desc, "global_batch": b, "seq_len": sq, "kv_len": skv, "heads_per_gpu": h,
+                "heads_total": global_h, "head_dim": 128, "parallelism": f"heads/{world}",
+                "l2": "inputs larger than L2 (q/k/v/dO/o/grad working set >> 126 MB); no flush",
+            },
+            "fwd_tflops": fwd_tf,
+            "bwd_tflops": bwd_tf,
+            "bwd_main_tflops": main_tf,
+            "fwd_frac_of_measured_peak": fwd_tf / peaks["bf16_tflops"],
+            "bwd_frac_of_measured_peak": bwd_tf / peaks["bf16_tflops"],
+            "frac_of_nominal_2250": {"fwd": fwd_tf / NOMINAL_BF16_TFLOPS, "bwd": bwd_tf / NOMINAL_BF16_TFLOPS},
+            "kernel_ms": kern_ms,
+            "roofline": {
+                "kernel": dominant, "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "peak_source": f"{peaks['source']} burst bf16 (MEASURED_PEAKS.json)" if peaks["source"] == "measured"
+                else "fallback 1.59 PFLOP/s",
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clk,
+            "gpu_launches": launches_per_step * args.steps,
+            "bwd_nsplit": plan["nsplit"],
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -27,7 +27,7 @@ FAST_SHAPES = [
     WanShape("cross", 1, 2, 2048, 257),    # I2V image branch length
 ]
 
-EDGE_SHAPES = [(1, 1), (65, 63), (128, 128), (129, 127), (200, 136), (257, 385)]
+EDGE_SHAPES = [(1, 2), (65, 63), (128, 128), (129, 127), (200, 136), (257, 385)]
 
 
 def _run(shape: WanShape, seed=0, std=1.0):
@@ -47,6 +47,15 @@ def test_bwd_fast(shape):
 @pytest.mark.parametrize("sq,skv", EDGE_SHAPES, ids=lambda x: str(x))
 def test_bwd_tile_edges(sq, skv):
     _run(WanShape("self" if sq == skv else "cross", 1, 1, sq, skv), seed=sq + 7 * skv)
+
+
+def test_bwd_single_key():
+    """skv = 1: P = 1, so dV = sum of dO over queries and dQ = dK = 0 exactly
+    in exact arithmetic (the oracle's dq/dk are fp32 rounding noise)."""
+    q, k, v, do = seeded(1, 300, 1, 2, seed=4)
+    grads, errs = bwd_vs_oracle(q, k, v, do)
+    assert errs["dv"]["rel_l2"] <= 4.5e-3
+    assert grads[0].float().abs().max().item() <= 1e-3 and grads[1].float().abs().max().item() <= 1e-3
 
 
 def test_bwd_batch_gt1():

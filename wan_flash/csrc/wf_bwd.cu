@@ -9,35 +9,50 @@
 //     dV  += P^T dO                     dK  += dS^T Q         dQ_blk = dS K
 // with dQ reduced into an fp32 accumulator, D and lse_log2 from the
 // preprocess kernel (+inf lse_log2 on pad query rows makes the m-tail
-// self-masking, bwd_sm90.py:167-172), the K tail masked by the row predicate
+// self-masking, bwd_sm90.py:167-172), the K tail masked by a row predicate
 // (:967-985), dK scaled once in the epilogue (:930) and dV never scaled.
 //
 // Blackwell schedule (one CTA per (KV block[, split], head, batch)):
-//   warps 0-3  "dS" warpgroup: thread = one KV row; P^T, dS^T, epilogue
-//   warps 4-7  "dQ" warpgroup: thread = one query row; drains dQ from TMEM
-//              and reduces it into dq_accum with vector fp32 reductions
-//   warp  8    tcgen05.mma issuer + TMEM owner
-//   warp  9    TMA producer (K/V once, Q/dO double-buffered)
+//   warps 0-3   elementwise WG A: thread = one KV row, query columns [0, 64)
+//   warps 4-7   elementwise WG B: thread = one KV row, query columns [64, 128)
+//   warps 8-11  dQ WG: thread = one query row; drains dQ from TMEM and
+//               reduces it into dq_accum with vector fp32 reductions
+//   warp  12    tcgen05.mma issuer + TMEM owner
+//   warp  13    TMA producer (K/V once; Q, dO, lse_log2, D double-buffered)
+//   warps 14-15 idle (complete warpgroup 3 so it can give registers back)
 //
-//   TMEM (512 columns): S^T [0,128) (P^T bf16 overwrites [0,64); dQ reuses
-//   all of it after the dV MMA has read P^T), dP^T [128,256), dV [256,384),
-//   dK [384,512).  dS^T goes to shared memory (128B-swizzled, [kv][q]); the
+//   TMEM (512 columns): S^T [0,128) -- P^T (bf16) overwrites [0,32) (WG A)
+//   and [64,96) (WG B), each inside the columns that WG has already read;
+//   dP^T [128,256) -- dQ reuses it once dS has been formed; dV [256,384);
+//   dK [384,512).  dS^T goes to shared memory (128B-swizzled, [kv][q]): the
 //   dK MMA reads it K-major and the dQ MMA reads the same bytes MN-major.
+//
+//   MMA order for query block u:  dV(u)  S(u+1)  dK(u)  dQ(u)  dP(u+1)
+//   S(u+1) only needs dV(u) to have read P^T(u) (in-order tensor pipe), so
+//   the next exponentials start while dK/dQ of this block run; dP(u+1)
+//   waits for the dQ warpgroup to have read dQ(u) out of the dP columns.
 #include "wf_common.cuh"
 #include "wf_kernels.h"
 
 namespace wf {
 
 namespace bwd {
-constexpr int kThreads = 320;
+constexpr int kThreads = 512;
+// register split (launch: 512 x 128 = 65536):
+//   2 elementwise WGs 128 x 144 + dQ WG 128 x 168 + WG3 128 x 56 = 65536
+constexpr uint32_t kRegsEw = 144;
+constexpr uint32_t kRegsDq = 168;
+constexpr uint32_t kRegsOther = 56;
 constexpr uint32_t kBoxBytes = 128 * 128;       // 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;  // 128 rows x 128 bf16
 constexpr uint32_t kOffK = 0;
 constexpr uint32_t kOffV = kOffK + kTileBytes;
-constexpr uint32_t kOffQ = kOffV + kTileBytes;     // 2 stages
+constexpr uint32_t kOffQ = kOffV + kTileBytes;       // 2 stages
 constexpr uint32_t kOffdO = kOffQ + 2 * kTileBytes;  // 2 stages
 constexpr uint32_t kOffdS = kOffdO + 2 * kTileBytes;
-constexpr uint32_t kOffBar = kOffdS + kTileBytes;
+constexpr uint32_t kOffLse = kOffdS + kTileBytes;    // 2 stages x 128 fp32
+constexpr uint32_t kOffD = kOffLse + 2 * 512;        // 2 stages x 128 fp32
+constexpr uint32_t kOffBar = kOffD + 2 * 512;
 constexpr int kBarKvFull = 0;
 constexpr int kBarQdoFull = 1;   // + stage
 constexpr int kBarQdoEmpty = 3;  // + stage
@@ -54,20 +69,21 @@ constexpr int kNumBars = 14;
 constexpr uint32_t kOffTmemHolder = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemHolder + 4;
 constexpr uint32_t kSmemUsed = kOffAbort + 4;
-constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + alignment slack
-static_assert(kSmemBytes <= 232448, "backward shared memory exceeds the sm_100 per-CTA limit");
+constexpr uint32_t kSmemLimit = 232448;  // sm_100 opt-in maximum per CTA
+// Request what fits: the base is re-aligned to 1024 B at run time and the
+// kernel checks that the aligned layout still fits (it normally needs no pad).
+constexpr uint32_t kSmemBytes = (kSmemUsed + 1024 <= kSmemLimit) ? kSmemUsed + 1024 : kSmemLimit;
+static_assert(kSmemUsed <= kSmemLimit, "backward shared memory exceeds the sm_100 per-CTA limit");
 }  // namespace bwd
 
 size_t bwd_smem_bytes() { return bwd::kSmemBytes; }
 
-enum : uint32_t { kRoleDs = 11, kRoleDq = 12, kRoleBwdMma = 13, kRoleBwdLoad = 14, kRoleEpi = 15 };
+enum : uint32_t { kRoleEw = 11, kRoleDq = 12, kRoleBwdMma = 13, kRoleBwdLoad = 14, kRoleEpi = 15 };
 
-__device__ __forceinline__ float4 ldg_f4(const float* p) {
-  float4 v;
-  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(p));
-  return v;
+__device__ __forceinline__ uint32_t dynamic_smem_size() {
+  uint32_t r;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
 }
 
 __global__ void __launch_bounds__(bwd::kThreads, 1)
@@ -76,7 +92,13 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
                        BwdParams p) {
   using namespace bwd;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uintptr_t raw = reinterpret_cast<uintptr_t>(smem_raw);
+  uint8_t* smem = reinterpret_cast<uint8_t*>((raw + 1023) & ~uintptr_t(1023));
+  if ((uint32_t)(reinterpret_cast<uintptr_t>(smem) - raw) + kSmemUsed > dynamic_smem_size()) {
+    // the aligned layout does not fit: report and leave (uniform for the CTA)
+    if (threadIdx.x == 0) atomicCAS(&g_err_code, 0u, (unsigned)WF_ERR_SMEM_ALIGN);
+    return;
+  }
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + kOffBar;
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
@@ -97,12 +119,14 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   const size_t bh = (size_t)b * p.h + h;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bar(i), (i == kBarPReady || i == kBarDsReady || i == kBarDqDrained) ? 128u : 1u);
+    for (int i = 0; i < kNumBars; ++i) {
+      const bool ew = (i == kBarPReady || i == kBarDsReady);
+      mbar_init(bar(i), ew ? 256u : (i == kBarDqDrained ? 128u : 1u));
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tmem_alloc(smem_u32(tmem_holder), 512);
     tmem_relinquish();
   }
@@ -111,7 +135,10 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 9) {
+  if (warp >= 14) {
+    regs_dec<kRegsOther>();  // idle warps of warpgroup 3
+  } else if (warp == 13) {
+    regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -127,13 +154,16 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       for (int u = 0; u < cnt; ++u) {
         const int st = u & 1, use = u >> 1;
         if (use > 0 && !mbar_wait(bar(kBarQdoEmpty + st), (use - 1) & 1, abort_flag, kRoleBwdLoad, 3 + st)) break;
-        const int m = (m_begin + u) * 128;
-        mbar_expect_tx(bar(kBarQdoFull + st), 2 * kTileBytes);
+        const int m = m_begin + u;
+        const uint32_t full = bar(kBarQdoFull + st);
+        mbar_expect_tx(full, 2 * kTileBytes + 1024);
         for (int x = 0; x < 2; ++x) {
-          tma_load_4d(sbase + kOffQ + st * kTileBytes + x * kBoxBytes, &tm_q, bar(kBarQdoFull + st), x * 64, m, h, b);
-          tma_load_4d(sbase + kOffdO + st * kTileBytes + x * kBoxBytes, &tm_do, bar(kBarQdoFull + st), x * 64, m, h,
-                      b);
+          tma_load_4d(sbase + kOffQ + st * kTileBytes + x * kBoxBytes, &tm_q, full, x * 64, m * 128, h, b);
+          tma_load_4d(sbase + kOffdO + st * kTileBytes + x * kBoxBytes, &tm_do, full, x * 64, m * 128, h, b);
         }
+        const size_t row0 = bh * (size_t)p.sq_rounded + (size_t)m * 128;
+        bulk_load(sbase + kOffLse + st * 512, p.lse_log2 + row0, 512, full);
+        bulk_load(sbase + kOffD + st * 512, p.dpsum + row0, 512, full);
         issued[st] = use + 1;
       }
       if (*abort_flag) {
@@ -142,95 +172,119 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           if (issued[st] > 0) mbar_wait_drain(bar(kBarQdoFull + st), (issued[st] - 1) & 1);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == 12) {
+    regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
       constexpr uint32_t id_kk = idesc_bf16(128, 128, 0, 0);  // A, B K-major
       constexpr uint32_t id_kb = idesc_bf16(128, 128, 0, 1);  // A K-major (or TMEM), B MN-major
       constexpr uint32_t id_mm = idesc_bf16(128, 128, 1, 1);  // A, B MN-major
       const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
-      const uint32_t sK = sbase + kOffK, sV = sbase + kOffV, sdS = sbase + kOffdS;
-      bool ok = mbar_wait(bar(kBarKvFull), 0, abort_flag, kRoleBwdMma, 0);
-      tc_fence_after();
+      // K-major operand descriptors advance 32 B per 16-element K step inside
+      // a 64-column box and 16 KB to the next box; MN-major ones use the 16 KB
+      // box stride as LBO and advance 2 KB per 16 rows of K.  Offsets are
+      // added to the encoded start-address field (addr >> 4, 14 bits).
+      const uint64_t dK_k = sdesc(sbase + kOffK, 16, 1024);
+      const uint64_t dV_k = sdesc(sbase + kOffV, 16, 1024);
+      const uint64_t dS_k = sdesc(sbase + kOffdS, 16, 1024);
+      const uint64_t dK_mn = sdesc(sbase + kOffK, kBoxBytes, 1024);
+      const uint64_t dS_mn = sdesc(sbase + kOffdS, kBoxBytes, 1024);
+      auto koff = [](int ks) -> uint32_t { return (uint32_t)(((ks >> 2) * kBoxBytes + (ks & 3) * 32) >> 4); };
+      auto moff = [](int ks) -> uint32_t { return (uint32_t)((ks * 2048) >> 4); };
+      auto issue_s = [&](int st) {  // S^T = K Q^T
+        const uint64_t q_k = sdesc(sbase + kOffQ + st * kTileBytes, 16, 1024);
+#pragma unroll 1
+        for (int ks = 0; ks < 8; ++ks) mma_ss(tS, dK_k + koff(ks), q_k + koff(ks), id_kk, ks > 0);
+        mma_commit(bar(kBarSFull));
+      };
+      auto issue_dp = [&](int st) {  // dP^T = V dO^T
+        const uint64_t do_k = sdesc(sbase + kOffdO + st * kTileBytes, 16, 1024);
+#pragma unroll 1
+        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, dV_k + koff(ks), do_k + koff(ks), id_kk, ks > 0);
+        mma_commit(bar(kBarDpFull));
+      };
+      bool ok = mbar_wait(bar(kBarKvFull), 0, abort_flag, kRoleBwdMma, 0) &&
+                mbar_wait(bar(kBarQdoFull + 0), 0, abort_flag, kRoleBwdMma, 1);
+      if (ok) {
+        tc_fence_after();
+        issue_dp(0);
+        issue_s(0);
+      }
       for (int u = 0; u < cnt && ok; ++u) {
         const int st = u & 1;
-        const uint32_t sQ = sbase + kOffQ + st * kTileBytes, sdO = sbase + kOffdO + st * kTileBytes;
-        if (!(ok = mbar_wait(bar(kBarQdoFull + st), (u >> 1) & 1, abort_flag, kRoleBwdMma, 1 + st))) break;
-        tc_fence_after();
-        // dP^T = V dO^T  (the dP region was released when dS(u-1) was signalled)
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32);
-          mma_ss(tdP, sdesc(sV + off, 16, 1024), sdesc(sdO + off, 16, 1024), id_kk, ks > 0);
-        }
-        mma_commit(bar(kBarDpFull));
-        // S^T = K Q^T once dQ(u-1) has left the shared S/dQ columns
-        if (u > 0) {
-          if (!(ok = mbar_wait(bar(kBarDqDrained), (u - 1) & 1, abort_flag, kRoleBwdMma, 11))) break;
-          tc_fence_after();
-        }
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32);
-          mma_ss(tS, sdesc(sK + off, 16, 1024), sdesc(sQ + off, 16, 1024), id_kk, ks > 0);
-        }
-        mma_commit(bar(kBarSFull));
-        // dV += P^T dO   (P^T from TMEM)
+        // dV += P^T dO   (P^T from TMEM: query 0-63 in columns [0,32), 64-127 in [64,96))
         if (!(ok = mbar_wait(bar(kBarPReady), u & 1, abort_flag, kRoleBwdMma, 7))) break;
         tc_fence_after();
-#pragma unroll
+        const uint64_t do_mn = sdesc(sbase + kOffdO + st * kTileBytes, kBoxBytes, 1024);
+#pragma unroll 1
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdV, tS + ks * 8, sdesc(sdO + ks * 2048, kBoxBytes, 1024), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, do_mn + moff(ks), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+        // S^T(u+1): the S columns are free once dV(u) has read P^T(u)
+        if (u + 1 < cnt) {
+          if (!(ok = mbar_wait(bar(kBarQdoFull + ((u + 1) & 1)), ((u + 1) >> 1) & 1, abort_flag, kRoleBwdMma, 1)))
+            break;
+          tc_fence_after();
+          issue_s((u + 1) & 1);
+        }
         // dK += dS^T Q   (dS^T from smem, K-major)
         if (!(ok = mbar_wait(bar(kBarDsReady), u & 1, abort_flag, kRoleBwdMma, 8))) break;
         tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32);
-          mma_ss(tdK, sdesc(sdS + off, 16, 1024), sdesc(sQ + ks * 2048, kBoxBytes, 1024), id_kb,
-                 (u > 0 || ks > 0) ? 1u : 0u);
-        }
-        mma_commit(bar(kBarQdoEmpty + st));
-        // dQ_blk = dS K   (same dS bytes read MN-major), into the S^T columns
-#pragma unroll
+        const uint64_t q_mn = sdesc(sbase + kOffQ + st * kTileBytes, kBoxBytes, 1024);
+#pragma unroll 1
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tS, sdesc(sdS + ks * 2048, kBoxBytes, 1024), sdesc(sK + ks * 2048, kBoxBytes, 1024), id_mm, ks > 0);
+          mma_ss(tdK, dS_k + koff(ks), q_mn + moff(ks), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(bar(kBarQdoEmpty + st));
+        // dQ_blk = dS K   (same dS bytes read MN-major) into the dP^T columns
+#pragma unroll 1
+        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, dS_mn + moff(ks), dK_mn + moff(ks), id_mm, ks > 0);
         mma_commit(bar(kBarDqFull));
         mma_commit(bar(kBarDsEmpty));
+        // dP^T(u+1) once dQ(u) has been read out of those columns
+        if (u + 1 < cnt) {
+          if (!(ok = mbar_wait(bar(kBarDqDrained), u & 1, abort_flag, kRoleBwdMma, 11))) break;
+          tc_fence_after();
+          issue_dp((u + 1) & 1);
+        }
       }
       if (ok) mma_commit(bar(kBarDkvFull));
       mma_commit(bar(kBarDrain));
       mbar_wait_drain(bar(kBarDrain), 0);
     }
-  } else if (warp < 4) {
-    // ------------------------------------------------------- dS warpgroup
-    const int wq = warp;
-    const int r = wq * 32 + lane;  // KV row within the block
+  } else if (warp < 8) {
+    regs_inc<kRegsEw>();
+    // ---------------------------------------------- elementwise warpgroups
+    const int half = warp >> 2;   // 0: query columns [0,64), 1: [64,128)
+    const int wq = warp & 3;      // TMEM lane quadrant
+    const int r = wq * 32 + lane; // KV row within the block
     const bool kv_valid = (n0 + r) < p.skv;
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_base, tdP = tS + 128, tdV = tS + 256, tdK = tS + 384;
-    uint8_t* sdS = smem + kOffdS;
+    const uint32_t tS = tmem + lane_base + (uint32_t)(half * 64);
+    const uint32_t tdP = tmem + lane_base + 128u + (uint32_t)(half * 64);
     const float sl2 = p.scale_log2;
+    uint8_t* sdS = smem + kOffdS + half * kBoxBytes;
     bool ok = true;
     for (int u = 0; u < cnt; ++u) {
-      const size_t row0 = bh * (size_t)p.sq_rounded + (size_t)(m_begin + u) * 128;
-      const float* lse_blk = p.lse_log2 + row0;
-      const float* d_blk = p.dpsum + row0;
-      if (!(ok = mbar_wait(bar(kBarSFull), u & 1, abort_flag, kRoleDs, 5))) break;
+      const int st = u & 1;
+      const float* slse = reinterpret_cast<const float*>(smem + kOffLse + st * 512) + half * 64;
+      const float* sD = reinterpret_cast<const float*>(smem + kOffD + st * 512) + half * 64;
+      if (!(ok = mbar_wait(bar(kBarSFull), u & 1, abort_flag, kRoleEw, 5))) break;
+      // lse_log2 / D of this block arrived with Q/dO (already complete; this
+      // wait makes the bulk-copied bytes visible to these threads)
+      if (!(ok = mbar_wait(bar(kBarQdoFull + st), (u >> 1) & 1, abort_flag, kRoleEw, 1))) break;
       tc_fence_after();
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
+      uint32_t s[2][32];
+      tmem_ld32(tS, s[0]);
+      tmem_ld32(tS + 32, s[1]);
       tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
+      reg_fence32(s[0]);
+      reg_fence32(s[1]);
       // P^T = exp2(S^T * scale_log2 - lse_log2[q]); zero on K-tail rows
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-          const float4 L = ldg_f4(lse_blk + c * 32 + v * 4);
+          const float4 L = *reinterpret_cast<const float4*>(slse + c * 32 + v * 4);
           float pv[4];
           pv[0] = ex2_approx(fmaf(__uint_as_float(s[c][4 * v + 0]), sl2, -L.x));
           pv[1] = ex2_approx(fmaf(__uint_as_float(s[c][4 * v + 1]), sl2, -L.y));
@@ -250,80 +304,81 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tc_fence_before();
       mbar_arrive(bar(kBarPReady));
       // dS^T = P^T * (dP^T - D[q])
-      if (!(ok = mbar_wait(bar(kBarDpFull), u & 1, abort_flag, kRoleDs, 6))) break;
+      if (!(ok = mbar_wait(bar(kBarDpFull), u & 1, abort_flag, kRoleEw, 6))) break;
       tc_fence_after();
-      if (u > 0 && !(ok = mbar_wait(bar(kBarDsEmpty), (u - 1) & 1, abort_flag, kRoleDs, 9))) break;
+      uint32_t dp[2][32];
+      tmem_ld32(tdP, dp[0]);
+      tmem_ld32(tdP + 32, dp[1]);
+      tmem_wait_ld();
+      reg_fence32(dp[0]);
+      reg_fence32(dp[1]);
+      tc_fence_before();  // the dP columns are read; dQ(u) may overwrite them after dS_ready
+      if (u > 0 && !(ok = mbar_wait(bar(kBarDsEmpty), (u - 1) & 1, abort_flag, kRoleEw, 9))) break;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t dp[32];
-        tmem_ld32(tdP + c * 32, dp);
-        tmem_wait_ld();
-        reg_fence32(dp);
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-          const float4 D = ldg_f4(d_blk + c * 32 + v * 4);
-          const float d0 = __uint_as_float(s[c][4 * v + 0]) * (__uint_as_float(dp[4 * v + 0]) - D.x);
-          const float d1 = __uint_as_float(s[c][4 * v + 1]) * (__uint_as_float(dp[4 * v + 1]) - D.y);
-          const float d2 = __uint_as_float(s[c][4 * v + 2]) * (__uint_as_float(dp[4 * v + 2]) - D.z);
-          const float d3 = __uint_as_float(s[c][4 * v + 3]) * (__uint_as_float(dp[4 * v + 3]) - D.w);
+          const float4 D = *reinterpret_cast<const float4*>(sD + c * 32 + v * 4);
+          const float d0 = __uint_as_float(s[c][4 * v + 0]) * (__uint_as_float(dp[c][4 * v + 0]) - D.x);
+          const float d1 = __uint_as_float(s[c][4 * v + 1]) * (__uint_as_float(dp[c][4 * v + 1]) - D.y);
+          const float d2 = __uint_as_float(s[c][4 * v + 2]) * (__uint_as_float(dp[c][4 * v + 2]) - D.z);
+          const float d3 = __uint_as_float(s[c][4 * v + 3]) * (__uint_as_float(dp[c][4 * v + 3]) - D.w);
           pk[2 * v] = pack_bf16(d0, d1);
           pk[2 * v + 1] = pack_bf16(d2, d3);
         }
-        // row r of dS^T: q columns [32c, 32c+32) = 4 chunks of 16 B in sub-tile c/2
-        uint8_t* sub = sdS + (c >> 1) * kBoxBytes;
+        // row r of dS^T, query columns [64*half + 32c, +32): 4 chunks of 16 B
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
-          const uint32_t off = sw128_offset((uint32_t)r, (uint32_t)((c & 1) * 4 + v));
-          *reinterpret_cast<uint4*>(sub + off) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          const uint32_t off = sw128_offset((uint32_t)r, (uint32_t)(c * 4 + v));
+          *reinterpret_cast<uint4*>(sdS + off) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
       }
       fence_proxy_async_smem();
       mbar_arrive(bar(kBarDsReady));
     }
     // ----------------------------------------------------------- epilogue
+    // WG A writes dV (unscaled), WG B writes dK (scaled by softmax_scale)
     if (ok) ok = mbar_wait(bar(kBarDkvFull), 0, abort_flag, kRoleEpi, 12);
     if (ok) {
       tc_fence_after();
       const int kv = n0 + r;
+      const uint32_t tsrc = tmem + lane_base + (half ? 384u : 256u);
+      const float mul = half ? p.scale : 1.f;
+      void* dst = half ? p.dk : p.dv;
 #pragma unroll 1
-      for (int which = 0; which < 2; ++which) {  // 0 = dV (unscaled), 1 = dK (scaled)
-        const uint32_t tsrc = which ? tdK : tdV;
-        const float mul = which ? p.scale : 1.f;
-        void* dst = which ? p.dk : p.dv;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t a[32];
-          tmem_ld32(tsrc + c * 32, a);
-          tmem_wait_ld();
-          reg_fence32(a);
-          if (!p.accum_dkv) {
-            if (kv_valid) {
-              __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(dst) + (((size_t)b * p.skv + kv) * p.h + h) * 128;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t a[32];
+        tmem_ld32(tsrc + c * 32, a);
+        tmem_wait_ld();
+        reg_fence32(a);
+        if (!p.accum_dkv) {
+          if (kv_valid) {
+            __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(dst) + (((size_t)b * p.skv + kv) * p.h + h) * 128;
 #pragma unroll
-              for (int v = 0; v < 4; ++v)
-                st_global_v4(row + c * 32 + v * 8,
-                             pack_bf16(__uint_as_float(a[8 * v + 0]) * mul, __uint_as_float(a[8 * v + 1]) * mul),
-                             pack_bf16(__uint_as_float(a[8 * v + 2]) * mul, __uint_as_float(a[8 * v + 3]) * mul),
-                             pack_bf16(__uint_as_float(a[8 * v + 4]) * mul, __uint_as_float(a[8 * v + 5]) * mul),
-                             pack_bf16(__uint_as_float(a[8 * v + 6]) * mul, __uint_as_float(a[8 * v + 7]) * mul));
-            }
-          } else {
-            float* tile = reinterpret_cast<float*>(dst) + (bh * (size_t)p.n_blocks + nb) * 16384 + (size_t)r * 4;
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              red_add_v4(tile + (size_t)(c * 8 + g) * 512, __uint_as_float(a[4 * g + 0]) * mul,
-                         __uint_as_float(a[4 * g + 1]) * mul, __uint_as_float(a[4 * g + 2]) * mul,
-                         __uint_as_float(a[4 * g + 3]) * mul);
+            for (int v = 0; v < 4; ++v)
+              st_global_v4(row + c * 32 + v * 8,
+                           pack_bf16(__uint_as_float(a[8 * v + 0]) * mul, __uint_as_float(a[8 * v + 1]) * mul),
+                           pack_bf16(__uint_as_float(a[8 * v + 2]) * mul, __uint_as_float(a[8 * v + 3]) * mul),
+                           pack_bf16(__uint_as_float(a[8 * v + 4]) * mul, __uint_as_float(a[8 * v + 5]) * mul),
+                           pack_bf16(__uint_as_float(a[8 * v + 6]) * mul, __uint_as_float(a[8 * v + 7]) * mul));
           }
+        } else {
+          float* tile = reinterpret_cast<float*>(dst) + (bh * (size_t)p.n_blocks + nb) * 16384 + (size_t)r * 4;
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            red_add_v4(tile + (size_t)(c * 8 + g) * 512, __uint_as_float(a[4 * g + 0]) * mul,
+                       __uint_as_float(a[4 * g + 1]) * mul, __uint_as_float(a[4 * g + 2]) * mul,
+                       __uint_as_float(a[4 * g + 3]) * mul);
         }
       }
     }
   } else {
+    regs_inc<kRegsDq>();
     // ------------------------------------------------------- dQ warpgroup
     const int wq = warp & 3;
     const int r = wq * 32 + lane;  // query row within the block
-    const uint32_t tQ = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t tQ = tmem + ((uint32_t)(wq * 32) << 16) + 128u;  // dQ lives in the dP^T columns
     for (int u = 0; u < cnt; ++u) {
       if (!mbar_wait(bar(kBarDqFull), u & 1, abort_flag, kRoleDq, 10)) break;
       tc_fence_after();
@@ -350,7 +405,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) tmem_dealloc(tmem, 512);
+  if (warp == 12) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace wf

@@ -109,6 +109,18 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
   return true;
 }
 
+// Register reallocation between warpgroups (all 4 warps of a warpgroup must
+// execute the same instruction).  The block's pool is what it was launched
+// with: threads x launch registers.
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------------------
 // Named barriers (sub-CTA sync among warpgroups)
 // ---------------------------------------------------------------------------

@@ -14,6 +14,7 @@
 //   warps 4-7  softmax for query tile 1
 //   warp  8    tcgen05.mma issuer (one thread) + TMEM owner
 //   warp  9    TMA producer (one thread)
+//   warps 10-11 idle (complete warpgroup 2 so it can give registers back)
 //
 //   TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
 //   P_t (bf16, 64 columns) overwrites the first half of S_t once S_t is read.
@@ -30,7 +31,10 @@
 namespace wf {
 
 namespace fwd {
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// register split (launch: 384 x 168 = 64512): softmax WGs 2 x 128 x 224 + WG2 128 x 56 = 64512
+constexpr uint32_t kRegsSoftmax = 224;
+constexpr uint32_t kRegsOther = 56;
 constexpr int kKvSlots = 4;
 constexpr uint32_t kBoxBytes = 128 * 128;        // 128 rows x 64 bf16 (one 128B-swizzled box)
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;   // 128 rows x 128 bf16
@@ -100,7 +104,10 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 9) {
+  if (warp >= 10) {
+    regs_dec<kRegsOther>();  // idle warps of warpgroup 2
+  } else if (warp == 9) {
+    regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -137,6 +144,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       }
     }
   } else if (warp == 8) {
+    regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_bf16(128, 128, 0, 0);
@@ -204,6 +212,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       mbar_wait_drain(bar(kBarDrain), 0);
     }
   } else {
+    regs_inc<kRegsSoftmax>();
     // -------------------------------------------------------------- softmax
     const int t = warp >> 2;           // query tile
     const int wq = warp & 3;           // TMEM lane quadrant
@@ -237,11 +246,11 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       // row max (tree for ILP)
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[0][i]);
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = (c == 0 ? 8 : 0); i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(s[c][i]));
+        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(s[c][i]));
       float mnew = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                          fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float mnew_s = mnew * sl2;

@@ -47,7 +47,7 @@ __global__ void wf_convert_kernel(const float* __restrict__ accum, __nv_bfloat16
 size_t fwd_smem_bytes();
 size_t bwd_smem_bytes();
 
-constexpr int kFwdThreads = 320;
-constexpr int kBwdThreads = 320;
+constexpr int kFwdThreads = 384;
+constexpr int kBwdThreads = 512;
 
 }  // namespace wf

@@ -57,7 +57,19 @@ def _ptr(t: torch.Tensor):
     return ctypes.c_void_p(t.data_ptr())
 
 
+def _mark(marks, name):
+    """Record a CUDA event on the current stream (bench timing only)."""
+    if marks is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+
 def wan_flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    return _fwd_impl(q, k, v)
+
+
+def _fwd_impl(q, k, v, marks=None):
     assert q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
     assert q.dim() == 4 and k.dim() == 4 and v.dim() == 4
     b, sq, h, d = q.shape
@@ -76,8 +88,10 @@ def wan_flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     f = features.get()
     cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler], 0)
     with torch.cuda.device(q.device):
+        _mark(marks, "fwd")
         rc = _lib.lib().wf_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), b, sq, skv, h,
                                ctypes.byref(cfg), ctypes.c_void_p(_stream_ptr(q.device)))
+        _mark(marks, "end")
     _lib.check(rc)
     return o, lse
 
@@ -131,6 +145,10 @@ def wan_flash_bwd(
 ):
     """(b,s,h,d) bf16 q/k/v/o/do; lse (b,h,s_q) fp32 natural log ->
     (dq, dk, dv) bf16 (b,s,h,d)."""
+    return _bwd_impl(q, k, v, o, lse, do)
+
+
+def _bwd_impl(q, k, v, o, lse, do, marks=None):
     assert all(t.dtype == torch.bfloat16 for t in (q, k, v, o, do))
     assert lse.dtype == torch.float32
     b, sq, h, d = q.shape
@@ -169,15 +187,19 @@ def wan_flash_bwd(
     stream = ctypes.c_void_p(_stream_ptr(dev))
     cfg = _lib.BwdCfg(nsplit)
     with torch.cuda.device(dev):
+        _mark(marks, "bwd_pre")
         _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(lse_log2), _ptr(dq_accum),
                                 b, sq, sq_rounded, h, stream))
+        _mark(marks, "bwd_main")
         _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse_log2), _ptr(dpsum),
                                  _ptr(dq_accum), _ptr(main_dk), _ptr(main_dv), b, sq, skv, h,
                                  ctypes.byref(cfg), stream))
+        _mark(marks, "bwd_convert")
         _lib.check(L.wf_bwd_convert(_ptr(dq_accum), _ptr(dq), ctypes.c_float(1.0 / math.sqrt(d)), b, sq, h, stream))
         if nsplit > 1:
             _lib.check(L.wf_bwd_convert(_ptr(dk_accum), _ptr(dk), ctypes.c_float(1.0), b, skv, h, stream))
             _lib.check(L.wf_bwd_convert(_ptr(dv_accum), _ptr(dv), ctypes.c_float(1.0), b, skv, h, stream))
+        _mark(marks, "end")
     return dq, dk, dv
 
 
