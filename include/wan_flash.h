@@ -70,14 +70,15 @@ int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
            int h, const wf_fwd_cfg* cfg, void* stream);
 
 /*
- * Backward preprocess: dpsum = rowsum(o * dO) (fp32), lse_log2 = lse * log2(e)
- * (+inf on pad rows, -inf mapped to 0), and zero dq_accum.
+ * Backward preprocess: dpsum = rowsum(o * dO) (fp32), neg_lse_log2 =
+ * -lse * log2(e) (-inf on pad rows, lse == -inf mapped to 0; the reference's
+ * lse_log2 workspace, negated), and zero dq_accum.
  * Replaces `compiled[0](*pre_args, stream)` of wan_flash/interface.py:190
  * (WanFlashBwdPreprocessSm90, wan_flash/bwd_sm90.py:99-235).
- *   dpsum, lse_log2: (b, h, sq_rounded) fp32, sq_rounded = ceil(sq/128)*128
+ *   dpsum, neg_lse_log2: (b, h, sq_rounded) fp32, sq_rounded = ceil(sq/128)*128
  *   dq_accum: b*h*sq_rounded*128 fp32 in 128-row tiles, see wf_bwd_convert
  */
-int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* lse_log2,
+int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* neg_lse_log2,
                float* dq_accum, int b, int sq, int sq_rounded, int h, void* stream);
 
 /*
@@ -90,7 +91,7 @@ int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, fl
  *                in the tiled layout of dq_accum (skv_rounded =
  *                ceil(skv/128)*128), zeroed by the caller; dk is scaled.
  */
-int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, const float* lse_log2,
+int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, const float* neg_lse_log2,
                 const float* dpsum, float* dq_accum, void* dk, void* dv, int b, int sq, int skv, int h,
                 const wf_bwd_cfg* cfg, void* stream);
 

@@ -1,10 +1,12 @@
 // Memory-bound kernels of the backward chain: the preprocess (rowsum(O*dO),
-// lse -> lse*log2(e), zero the dQ accumulator) and the fp32-accumulator ->
+// lse -> -lse*log2(e), zero the dQ accumulator) and the fp32-accumulator ->
 // bf16 convert.  Both are plain coalesced loads/stores sized for HBM.
 //
 // Reference counterparts (Quarky93/wan-flash): WanFlashBwdPreprocessSm90,
 // wan_flash/bwd_sm90.py:99-235 (D at :195-217, zero dQaccum :219-228,
-// lse_log2 with +inf pad rows and -inf -> 0 at :230-235) and
+// lse_log2 with +inf pad rows and -inf -> 0 at :230-235; stored negated here,
+// so pad rows hold -inf and the main kernel needs one fused multiply-add per
+// exponent) and
 // WanFlashBwdPostprocessSm90, wan_flash/bwd_sm90.py:1140-1308.  The
 // accumulator here is stored in 128-row tiles of [32 groups of 4 columns]
 // [128 rows][4] (the order the backward main kernel reduces into), not the
@@ -33,8 +35,9 @@ __device__ __forceinline__ float bf16_dot2(uint32_t a, uint32_t b) {
 __global__ void __launch_bounds__(256) wf_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o,
                                                          const __nv_bfloat16* __restrict__ dO,
                                                          const float* __restrict__ lse, float* __restrict__ dpsum,
-                                                         float* __restrict__ lse_log2, float* __restrict__ dq_accum,
-                                                         int sq, int sq_rounded, int h_total) {
+                                                         float* __restrict__ neg_lse_log2,
+                                                         float* __restrict__ dq_accum, int sq, int sq_rounded,
+                                                         int h_total) {
   const int h = blockIdx.y, b = blockIdx.z;
   const size_t bh = (size_t)b * h_total + h;
   const int row0 = blockIdx.x * 64;
@@ -53,13 +56,13 @@ __global__ void __launch_bounds__(256) wf_bwd_pre_kernel(const __nv_bfloat16* __
 #pragma unroll
     for (int m = 8; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
     if (sub == 0) {
-      float l2 = INFINITY;  // pad rows: P = exp2(-inf) = 0
+      float nl2 = -INFINITY;  // pad rows: P = exp2(-inf) = 0
       if (s < sq) {
         const float l = lse[bh * sq + s];
-        l2 = (l == -INFINITY) ? 0.f : l * 1.4426950408889634f;
+        nl2 = (l == -INFINITY) ? 0.f : -(l * 1.4426950408889634f);
       }
       dpsum[bh * sq_rounded + s] = acc;
-      lse_log2[bh * sq_rounded + s] = l2;
+      neg_lse_log2[bh * sq_rounded + s] = nl2;
     }
   }
   // zero rows [row0, row0 + 64) of the tiled dQ accumulator

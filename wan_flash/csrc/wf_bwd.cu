@@ -4,12 +4,12 @@
 // Computes what the reference backward main kernel computes
 // (wan_flash/bwd_sm90.py of Quarky93/wan-flash, `_mma_m_block` :947-1046):
 // for one 128-row KV block it walks the query blocks and forms
-//     S^T  = K Q^T                      P^T = exp2(S^T * scale_log2 - lse_log2)
+//     S^T  = K Q^T                      P^T = exp2(S^T * scale_log2 - lse * log2(e))
 //     dP^T = V dO^T                     dS^T = P^T * (dP^T - D)
 //     dV  += P^T dO                     dK  += dS^T Q         dQ_blk = dS K
 // with dQ reduced into an fp32 accumulator, D and lse_log2 from the
-// preprocess kernel (+inf lse_log2 on pad query rows makes the m-tail
-// self-masking, bwd_sm90.py:167-172), the K tail masked by a row predicate
+// preprocess kernel (stored negated: -inf on pad query rows makes the m-tail
+// self-masking, as the +inf lse_log2 sentinel of bwd_sm90.py:167-172), the K tail masked by a row predicate
 // (:967-985), dK scaled once in the epilogue (:930) and dV never scaled.
 //
 // Blackwell schedule (one CTA per (KV block[, split], head, batch)):
@@ -18,7 +18,7 @@
 //   warps 8-11  dQ WG: thread = one query row; drains dQ from TMEM and
 //               reduces it into dq_accum with vector fp32 reductions
 //   warp  12    tcgen05.mma issuer + TMEM owner
-//   warp  13    TMA producer (K/V once; Q, dO, lse_log2, D double-buffered)
+//   warp  13    TMA producer (K/V once; Q, dO, -lse*log2(e), D double-buffered)
 //   warps 14-15 idle (complete warpgroup 3 so it can give registers back)
 //
 //   TMEM (512 columns): S^T [0,128) -- P^T (bf16) overwrites [0,32) (WG A)
@@ -39,9 +39,9 @@ namespace wf {
 namespace bwd {
 constexpr int kThreads = 512;
 // register split (launch: 512 x 128 = 65536):
-//   2 elementwise WGs 128 x 144 + dQ WG 128 x 168 + WG3 128 x 56 = 65536
-constexpr uint32_t kRegsEw = 144;
-constexpr uint32_t kRegsDq = 168;
+//   2 elementwise WGs 128 x 152 + dQ WG 128 x 152 + WG3 128 x 56 = 65536
+constexpr uint32_t kRegsEw = 152;
+constexpr uint32_t kRegsDq = 152;
 constexpr uint32_t kRegsOther = 56;
 constexpr uint32_t kBoxBytes = 128 * 128;       // 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;  // 128 rows x 128 bf16
@@ -50,7 +50,7 @@ constexpr uint32_t kOffV = kOffK + kTileBytes;
 constexpr uint32_t kOffQ = kOffV + kTileBytes;       // 2 stages
 constexpr uint32_t kOffdO = kOffQ + 2 * kTileBytes;  // 2 stages
 constexpr uint32_t kOffdS = kOffdO + 2 * kTileBytes;
-constexpr uint32_t kOffLse = kOffdS + kTileBytes;    // 2 stages x 128 fp32
+constexpr uint32_t kOffLse = kOffdS + kTileBytes;    // 2 stages x 128 fp32 (-lse * log2 e)
 constexpr uint32_t kOffD = kOffLse + 2 * 512;        // 2 stages x 128 fp32
 constexpr uint32_t kOffBar = kOffD + 2 * 512;
 constexpr int kBarKvFull = 0;
@@ -77,6 +77,9 @@ static_assert(kSmemUsed <= kSmemLimit, "backward shared memory exceeds the sm_10
 }  // namespace bwd
 
 size_t bwd_smem_bytes() { return bwd::kSmemBytes; }
+
+// Fraction of exponent pairs evaluated by the FMA-pipe polynomial (0 = none).
+constexpr int kBwdPolyEvery = 0;
 
 enum : uint32_t { kRoleEw = 11, kRoleDq = 12, kRoleBwdMma = 13, kRoleBwdLoad = 14, kRoleEpi = 15 };
 
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           tma_load_4d(sbase + kOffdO + st * kTileBytes + x * kBoxBytes, &tm_do, full, x * 64, m * 128, h, b);
         }
         const size_t row0 = bh * (size_t)p.sq_rounded + (size_t)m * 128;
-        bulk_load(sbase + kOffLse + st * 512, p.lse_log2 + row0, 512, full);
+        bulk_load(sbase + kOffLse + st * 512, p.neg_lse_log2 + row0, 512, full);
         bulk_load(sbase + kOffD + st * 512, p.dpsum + row0, 512, full);
         issued[st] = use + 1;
       }
@@ -182,25 +185,25 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
       // K-major operand descriptors advance 32 B per 16-element K step inside
       // a 64-column box and 16 KB to the next box; MN-major ones use the 16 KB
-      // box stride as LBO and advance 2 KB per 16 rows of K.  Offsets are
-      // added to the encoded start-address field (addr >> 4, 14 bits).
+      // box stride as LBO and advance 2 KB per 16 rows of K (desc_add adds
+      // the offset to the encoded start-address field).
       const uint64_t dK_k = sdesc(sbase + kOffK, 16, 1024);
       const uint64_t dV_k = sdesc(sbase + kOffV, 16, 1024);
       const uint64_t dS_k = sdesc(sbase + kOffdS, 16, 1024);
       const uint64_t dK_mn = sdesc(sbase + kOffK, kBoxBytes, 1024);
       const uint64_t dS_mn = sdesc(sbase + kOffdS, kBoxBytes, 1024);
-      auto koff = [](int ks) -> uint32_t { return (uint32_t)(((ks >> 2) * kBoxBytes + (ks & 3) * 32) >> 4); };
-      auto moff = [](int ks) -> uint32_t { return (uint32_t)((ks * 2048) >> 4); };
+      auto koff = [](int ks) -> uint32_t { return (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32); };
+      auto moff = [](int ks) -> uint32_t { return (uint32_t)(ks * 2048); };
       auto issue_s = [&](int st) {  // S^T = K Q^T
         const uint64_t q_k = sdesc(sbase + kOffQ + st * kTileBytes, 16, 1024);
-#pragma unroll 1
-        for (int ks = 0; ks < 8; ++ks) mma_ss(tS, dK_k + koff(ks), q_k + koff(ks), id_kk, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) mma_ss(tS, desc_add(dK_k, koff(ks)), desc_add(q_k, koff(ks)), id_kk, ks > 0);
         mma_commit(bar(kBarSFull));
       };
       auto issue_dp = [&](int st) {  // dP^T = V dO^T
         const uint64_t do_k = sdesc(sbase + kOffdO + st * kTileBytes, 16, 1024);
-#pragma unroll 1
-        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, dV_k + koff(ks), do_k + koff(ks), id_kk, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, desc_add(dV_k, koff(ks)), desc_add(do_k, koff(ks)), id_kk, ks > 0);
         mma_commit(bar(kBarDpFull));
       };
       bool ok = mbar_wait(bar(kBarKvFull), 0, abort_flag, kRoleBwdMma, 0) &&
@@ -216,9 +219,9 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         if (!(ok = mbar_wait(bar(kBarPReady), u & 1, abort_flag, kRoleBwdMma, 7))) break;
         tc_fence_after();
         const uint64_t do_mn = sdesc(sbase + kOffdO + st * kTileBytes, kBoxBytes, 1024);
-#pragma unroll 1
+#pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, do_mn + moff(ks), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(do_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
         // S^T(u+1): the S columns are free once dV(u) has read P^T(u)
         if (u + 1 < cnt) {
           if (!(ok = mbar_wait(bar(kBarQdoFull + ((u + 1) & 1)), ((u + 1) >> 1) & 1, abort_flag, kRoleBwdMma, 1)))
@@ -230,13 +233,13 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         if (!(ok = mbar_wait(bar(kBarDsReady), u & 1, abort_flag, kRoleBwdMma, 8))) break;
         tc_fence_after();
         const uint64_t q_mn = sdesc(sbase + kOffQ + st * kTileBytes, kBoxBytes, 1024);
-#pragma unroll 1
+#pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdK, dS_k + koff(ks), q_mn + moff(ks), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+          mma_ss(tdK, desc_add(dS_k, koff(ks)), desc_add(q_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
         mma_commit(bar(kBarQdoEmpty + st));
         // dQ_blk = dS K   (same dS bytes read MN-major) into the dP^T columns
-#pragma unroll 1
-        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, dS_mn + moff(ks), dK_mn + moff(ks), id_mm, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, desc_add(dS_mn, moff(ks)), desc_add(dK_mn, moff(ks)), id_mm, ks > 0);
         mma_commit(bar(kBarDqFull));
         mma_commit(bar(kBarDsEmpty));
         // dP^T(u+1) once dQ(u) has been read out of those columns
@@ -261,14 +264,15 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     const uint32_t tS = tmem + lane_base + (uint32_t)(half * 64);
     const uint32_t tdP = tmem + lane_base + 128u + (uint32_t)(half * 64);
     const float sl2 = p.scale_log2;
+    const uint64_t sl2x2 = f2_pack(sl2, sl2);
     uint8_t* sdS = smem + kOffdS + half * kBoxBytes;
     bool ok = true;
     for (int u = 0; u < cnt; ++u) {
       const int st = u & 1;
-      const float* slse = reinterpret_cast<const float*>(smem + kOffLse + st * 512) + half * 64;
+      const float* snl = reinterpret_cast<const float*>(smem + kOffLse + st * 512) + half * 64;
       const float* sD = reinterpret_cast<const float*>(smem + kOffD + st * 512) + half * 64;
       if (!(ok = mbar_wait(bar(kBarSFull), u & 1, abort_flag, kRoleEw, 5))) break;
-      // lse_log2 / D of this block arrived with Q/dO (already complete; this
+      // -lse*log2(e) / D of this block arrived with Q/dO (already complete; this
       // wait makes the bulk-copied bytes visible to these threads)
       if (!(ok = mbar_wait(bar(kBarQdoFull + st), (u >> 1) & 1, abort_flag, kRoleEw, 1))) break;
       tc_fence_after();
@@ -278,25 +282,26 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tmem_wait_ld();
       reg_fence32(s[0]);
       reg_fence32(s[1]);
-      // P^T = exp2(S^T * scale_log2 - lse_log2[q]); zero on K-tail rows
+      // P^T = 2^(S^T * scale_log2 + neg_lse_log2[q]) (MUFU; with kBwdPolyEvery > 0
+      // one pair in kBwdPolyEvery uses the FMA-pipe polynomial).  Rows past the K
+      // tail are zeroed.
+      uint64_t pp[2][16];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-          const float4 L = *reinterpret_cast<const float4*>(slse + c * 32 + v * 4);
-          float pv[4];
-          pv[0] = ex2_approx(fmaf(__uint_as_float(s[c][4 * v + 0]), sl2, -L.x));
-          pv[1] = ex2_approx(fmaf(__uint_as_float(s[c][4 * v + 1]), sl2, -L.y));
-          pv[2] = ex2_approx(fmaf(__uint_as_float(s[c][4 * v + 2]), sl2, -L.z));
-          pv[3] = ex2_approx(fmaf(__uint_as_float(s[c][4 * v + 3]), sl2, -L.w));
+          const float4 L = *reinterpret_cast<const float4*>(snl + c * 32 + v * 4);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (!kv_valid) pv[e] = 0.f;
-            s[c][4 * v + e] = __float_as_uint(pv[e]);
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * v + e;
+            const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2,
+                                      e ? f2_pack(L.z, L.w) : f2_pack(L.x, L.y));
+            pp[c][i] = (kBwdPolyEvery > 0 && (i % kBwdPolyEvery) == kBwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
+            float p0, p1;
+            f2_unpack(pp[c][i], p0, p1);
+            pk[i] = kv_valid ? pack_bf16(p0, p1) : 0u;
           }
-          pk[2 * v] = pack_bf16(pv[0], pv[1]);
-          pk[2 * v + 1] = pack_bf16(pv[2], pv[3]);
         }
         tmem_st16(tS + c * 16, pk);
       }
@@ -314,18 +319,22 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       reg_fence32(dp[1]);
       tc_fence_before();  // the dP columns are read; dQ(u) may overwrite them after dS_ready
       if (u > 0 && !(ok = mbar_wait(bar(kBarDsEmpty), (u - 1) & 1, abort_flag, kRoleEw, 9))) break;
+      const uint64_t m1x2 = f2_pack(-1.f, -1.f);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const float4 D = *reinterpret_cast<const float4*>(sD + c * 32 + v * 4);
-          const float d0 = __uint_as_float(s[c][4 * v + 0]) * (__uint_as_float(dp[c][4 * v + 0]) - D.x);
-          const float d1 = __uint_as_float(s[c][4 * v + 1]) * (__uint_as_float(dp[c][4 * v + 1]) - D.y);
-          const float d2 = __uint_as_float(s[c][4 * v + 2]) * (__uint_as_float(dp[c][4 * v + 2]) - D.z);
-          const float d3 = __uint_as_float(s[c][4 * v + 3]) * (__uint_as_float(dp[c][4 * v + 3]) - D.w);
-          pk[2 * v] = pack_bf16(d0, d1);
-          pk[2 * v + 1] = pack_bf16(d2, d3);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * v + e;
+            const uint64_t dpp = f2_pack(__uint_as_float(dp[c][2 * i]), __uint_as_float(dp[c][2 * i + 1]));
+            const uint64_t t = f2_fma(e ? f2_pack(D.z, D.w) : f2_pack(D.x, D.y), m1x2, dpp);
+            float d0, d1;
+            f2_unpack(f2_mul(pp[c][i], t), d0, d1);
+            pk[i] = kv_valid ? pack_bf16(d0, d1) : 0u;
+          }
         }
         // row r of dS^T, query columns [64*half + 32c, +32): 4 chunks of 16 B
 #pragma unroll
@@ -346,7 +355,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       const uint32_t tsrc = tmem + lane_base + (half ? 384u : 256u);
       const float mul = half ? p.scale : 1.f;
       void* dst = half ? p.dk : p.dv;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t a[32];
         tmem_ld32(tsrc + c * 32, a);

@@ -195,41 +195,41 @@ int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
   return launch_check("wf_fwd launch");
 }
 
-int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* lse_log2, float* dq_accum, int b,
+int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* neg_lse_log2, float* dq_accum, int b,
                int sq, int sq_rounded, int h, void* stream) {
   int rc = check_dims(b, sq, sq_rounded, h);
   if (rc) return rc;
   if (sq_rounded != (sq + 127) / 128 * 128) return fail(WF_ERR_INVALID_ARG, "sq_rounded must be ceil(sq/128)*128");
   if (b == 0 || sq == 0 || h == 0) return WF_OK;
-  if (!o || !dO || !lse || !dpsum || !lse_log2 || !dq_accum) return fail(WF_ERR_INVALID_ARG, "null pointer");
-  if (!aligned16(o) || !aligned16(dO) || !aligned16(dpsum) || !aligned16(lse_log2) || !aligned16(dq_accum))
-    return fail(WF_ERR_MISALIGNED, "o/dO/dpsum/lse_log2/dq_accum must be 16-byte aligned");
+  if (!o || !dO || !lse || !dpsum || !neg_lse_log2 || !dq_accum) return fail(WF_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(o) || !aligned16(dO) || !aligned16(dpsum) || !aligned16(neg_lse_log2) || !aligned16(dq_accum))
+    return fail(WF_ERR_MISALIGNED, "o/dO/dpsum/neg_lse_log2/dq_accum must be 16-byte aligned");
   int dev;
   if ((rc = device_setup(&dev))) return rc;
   dim3 grid(sq_rounded / 64, h, b);
   wf_bwd_pre_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(dO), lse, dpsum, lse_log2,
+      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(dO), lse, dpsum, neg_lse_log2,
       dq_accum, sq, sq_rounded, h);
   return launch_check("wf_bwd_pre launch");
 }
 
-int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, const float* lse_log2,
+int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, const float* neg_lse_log2,
                 const float* dpsum, float* dq_accum, void* dk, void* dv, int b, int sq, int skv, int h,
                 const wf_bwd_cfg* cfg, void* stream) {
   int rc = check_dims(b, sq, skv, h);
   if (rc) return rc;
   if (b == 0 || h == 0 || skv == 0) return WF_OK;
   if (sq == 0) return fail(WF_ERR_UNSUPPORTED, "sq == 0: the caller must zero dk/dv");
-  if (!q || !k || !v || !dO || !lse_log2 || !dpsum || !dq_accum || !dk || !dv)
+  if (!q || !k || !v || !dO || !neg_lse_log2 || !dpsum || !dq_accum || !dk || !dv)
     return fail(WF_ERR_INVALID_ARG, "null pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dO) || !aligned16(lse_log2) ||
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dO) || !aligned16(neg_lse_log2) ||
       !aligned16(dpsum) || !aligned16(dq_accum) || !aligned16(dk) || !aligned16(dv))
     return fail(WF_ERR_MISALIGNED, "all buffers must be 16-byte aligned");
   const int nsplit = cfg ? cfg->nsplit : 1;
   int dev;
   if ((rc = device_setup(&dev))) return rc;
   BwdParams p;
-  p.lse_log2 = lse_log2;
+  p.neg_lse_log2 = neg_lse_log2;
   p.dpsum = dpsum;
   p.dq_accum = dq_accum;
   p.dk = dk;

@@ -231,6 +231,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15]));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -268,6 +283,15 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, ui
   return d;
 }
 
+// Descriptor + byte offset (>> 4 into the start-address field).  Opaque to the
+// optimiser on purpose: unrolled MMA issue loops would otherwise hoist every
+// loop-invariant descriptor into registers of the (register-poor) MMA warp.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) {
+  uint64_t r;
+  asm volatile("add.u64 %0, %1, %2;" : "=l"(r) : "l"(d), "l"((uint64_t)(byte_off >> 4)));
+  return r;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
 // a_mn / b_mn: 1 when the operand is MN-major in shared memory.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn) {
@@ -288,6 +312,74 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (one instruction for two lanes of math on sm_100)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of floats on the FMA/ALU pipes (no MUFU):
+// Cody-Waite reduction x = j + f, j = rint(x) via the 1.5 * 2^23 rounding
+// constant, f in [-1/2, 1/2]; p(f) is a degree-5 polynomial minimising the
+// relative error to 2^f on [-1/2, 1/2] (Remez exchange fit, coefficients from
+// wan_flash/csrc/fit_exp2_poly.py; max relative error 2.3e-7 in fp32); the
+// result is p(f) with j added to its exponent field.  Inputs are clamped to
+// >= -126 so the exponent stays normal; -inf gives ~2^-126 (weight zero in bf16).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  const uint64_t xc = f2_pack(x0, x1);
+  const uint64_t t = f2_add(xc, f2_pack(kRound, kRound));
+  const uint64_t j = f2_add(t, f2_pack(-kRound, -kRound));
+  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), xc);
+  uint64_t pl = f2_fma(f2_pack(1.327647245e-03f, 1.327647245e-03f), f, f2_pack(9.675540961e-03f, 9.675540961e-03f));
+  pl = f2_fma(pl, f, f2_pack(5.550713092e-02f, 5.550713092e-02f));
+  pl = f2_fma(pl, f, f2_pack(2.402212024e-01f, 2.402212024e-01f));
+  pl = f2_fma(pl, f, f2_pack(6.931469440e-01f, 6.931469440e-01f));
+  pl = f2_fma(pl, f, f2_pack(1.000000119e+00f, 1.000000119e+00f));
+  float t0, t1, p0, p1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(pl, p0, p1);
+  p0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  return f2_pack(p0, p1);
+}
+// 2^x for a pair on the MUFU pipe.
+__device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x) {
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  return f2_pack(ex2_approx(x0), ex2_approx(x1));
+}
+
 // Pack two fp32 into bf16x2 with round-to-nearest-even: `lo` in bits 0-15.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;

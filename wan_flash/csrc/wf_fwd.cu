@@ -32,9 +32,9 @@ namespace wf {
 
 namespace fwd {
 constexpr int kThreads = 384;
-// register split (launch: 384 x 168 = 64512): softmax WGs 2 x 128 x 224 + WG2 128 x 56 = 64512
-constexpr uint32_t kRegsSoftmax = 224;
-constexpr uint32_t kRegsOther = 56;
+// register split (launch: 384 x 168 = 64512): softmax WGs 2 x 128 x 208 + WG2 128 x 88 = 64512
+constexpr uint32_t kRegsSoftmax = 208;
+constexpr uint32_t kRegsOther = 88;
 constexpr int kKvSlots = 4;
 constexpr uint32_t kBoxBytes = 128 * 128;        // 128 rows x 64 bf16 (one 128B-swizzled box)
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;   // 128 rows x 128 bf16
@@ -60,6 +60,52 @@ size_t fwd_smem_bytes() { return fwd::kSmemBytes; }
 
 // role ids recorded on a wait timeout
 enum : uint32_t { kRoleSoftmax0 = 1, kRoleSoftmax1 = 2, kRoleMma = 3, kRoleLoad = 4 };
+
+// Exponentials of one 128-column block of scores for this thread's row:
+// P = 2^(s * scale_log2 - m) stored to TMEM as bf16 pairs (chunk by chunk,
+// over the already-read S columns), the fp32 row sum returned in `sum_out`
+// and, with kWithMax, the block's raw row max in `max_out`.  Packed f32x2
+// math and a 3-input max keep the instruction count low: the softmax warps
+// share their SMSPs with the MMA-issuing warp, whose issue rate sets the
+// tensor pipe's.  kFwdPolyEvery > 0 routes one pair in kFwdPolyEvery through the
+// FMA-pipe polynomial exp2 instead of MUFU (off by default: on B200 it costs
+// more issue slots than the MUFU time it saves here).
+constexpr int kFwdPolyEvery = 0;
+
+template <bool kWithMax>
+__device__ __forceinline__ void fwd_exp_block(const uint32_t (&s)[4][32], uint32_t tS, float sl2, float neg_m,
+                                              float& sum_out, float& max_out) {
+  const uint64_t sl2x2 = f2_pack(sl2, sl2);
+  const uint64_t negx2 = f2_pack(neg_m, neg_m);
+  uint64_t acc[4];
+  float mx[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc[i] = f2_pack(0.f, 0.f);
+    mx[i] = -INFINITY;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float s0 = __uint_as_float(s[c][2 * i]), s1 = __uint_as_float(s[c][2 * i + 1]);
+      if (kWithMax) mx[i & 3] = fmax3(mx[i & 3], s0, s1);
+      const uint64_t x = f2_fma(f2_pack(s0, s1), sl2x2, negx2);
+      const uint64_t pp =
+          (kFwdPolyEvery > 0 && (i % kFwdPolyEvery) == kFwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
+      acc[i & 3] = f2_add(acc[i & 3], pp);
+      float p0, p1;
+      f2_unpack(pp, p0, p1);
+      pk[i] = pack_bf16(p0, p1);
+    }
+    tmem_st16(tS + c * 16, pk);
+  }
+  float a0, a1;
+  f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), a0, a1);
+  sum_out = a0 + a1;
+  max_out = kWithMax ? fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) : 0.f;
+}
 
 __global__ void __launch_bounds__(fwd::kThreads, 1)
     wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -155,22 +201,21 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       tc_fence_after();
       auto issue_s = [&](int t, int slot_k) {
         const uint32_t d = tmem + (uint32_t)(t * 128);
+        const uint64_t a0 = sdesc(sQ + t * kTileBytes, 16, 1024);
+        const uint64_t b0 = sdesc(sKV + slot_k * kTileBytes, 16, 1024);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t off = (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32);
-          const uint64_t a = sdesc(sQ + t * kTileBytes + off, 16, 1024);
-          const uint64_t bd = sdesc(sKV + slot_k * kTileBytes + off, 16, 1024);
-          mma_ss(d, a, bd, idesc_qk, ks > 0);
+          mma_ss(d, desc_add(a0, off), desc_add(b0, off), idesc_qk, ks > 0);
         }
       };
       auto issue_pv = [&](int t, int slot_v, bool acc) {
         const uint32_t d = tmem + 256u + (uint32_t)(t * 128);
         const uint32_t a = tmem + (uint32_t)(t * 128);  // P_t: bf16 pairs in S_t columns [0, 64)
+        const uint64_t b0 = sdesc(sKV + slot_v * kTileBytes, kBoxBytes, 1024);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint64_t bd = sdesc(sKV + slot_v * kTileBytes + ks * 2048, kBoxBytes, 1024);
-          mma_ts(d, a + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ts(d, a + ks * 8, desc_add(b0, (uint32_t)(ks * 2048)), idesc_pv, (acc || ks > 0) ? 1u : 0u);
       };
       for (int it = 0; it < n_blocks && ok; ++it) {
         const int uk = 2 * it, slot_k = uk % kKvSlots;
@@ -236,63 +281,55 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
-      if (it == 0 && tail_valid < 128) {
+      float bsum, bmax;
+      if (it == 0) {
+        // first (ragged tail) block: mask, reduce the row max, then exponentiate
+        if (tail_valid < 128) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
-      }
-      // row max (tree for ILP)
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(s[c][i]));
-      float mnew = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float mnew_s = mnew * sl2;
-      float factor = 1.f;
-      bool need = false;
-      if (it == 0) {
-        m_s = mnew_s;
-      } else if (mnew_s - m_s > thr) {
-        factor = ex2_approx(m_s - mnew_s);
-        l *= factor;
-        m_s = mnew_s;
-        need = true;
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        // O_t holds the sum through block it-1 (its PV completed before S_t(it) was signalled)
+          for (int i = 0; i < 16; ++i)
+            mx[i & 3] = fmax3(mx[i & 3], __uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1]));
+        m_s = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+        fwd_exp_block<false>(s, tS, sl2, -m_s, bsum, bmax);
+        l = bsum;
+      } else {
+        // speculative: exponentiate against the running reference max while
+        // reducing this block's max; redo only if the max moved past the
+        // rescale threshold (rare after the first blocks)
+        fwd_exp_block<true>(s, tS, sl2, -m_s, bsum, bmax);
+        const float mnew_s = bmax * sl2;
+        const bool need = mnew_s - m_s > thr;
+        if (__any_sync(0xffffffffu, need)) {
+          const float factor = need ? ex2_approx(m_s - mnew_s) : 1.f;
+          if (need) {
+            l *= factor;
+            m_s = mnew_s;
+          }
+          // O_t holds the sum through block it-1 (its PV completed before S_t(it) was signalled)
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-          reg_fence32(o);
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o[16];
+            tmem_ld16(tO + c * 16, o);
+            tmem_wait_ld();
+            reg_fence16(o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          tmem_st32(tO + c * 32, o);
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            tmem_st16(tO + c * 16, o);
+          }
+          tmem_wait_st();
+          fwd_exp_block<false>(s, tS, sl2, -m_s, bsum, bmax);
         }
-      }
-      const float neg = -m_s;
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * i]), sl2, neg));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * i + 1]), sl2, neg));
-          sum[i & 3] += p0 + p1;
-          pk[i] = pack_bf16(p0, p1);
-        }
-        tmem_st16(tS + c * 16, pk);
+        l += bsum;
       }
       tmem_wait_st();
-      l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
       tc_fence_before();
       mbar_arrive(bar(kBarPFull + t));
     }

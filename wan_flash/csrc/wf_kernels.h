@@ -19,7 +19,7 @@ struct FwdParams {
 };
 
 struct BwdParams {
-  const float* lse_log2;   // (b, h, sq_rounded)
+  const float* neg_lse_log2;  // (b, h, sq_rounded): -lse * log2(e), -inf on pad rows
   const float* dpsum;      // (b, h, sq_rounded)
   float* dq_accum;         // tiled, b*h*sq_rounded*128
   void* dk;                // bf16 (b, skv, h, 128) or fp32 tiled accumulator
@@ -39,7 +39,7 @@ __global__ void wf_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q, con
                                    BwdParams p);
 __global__ void wf_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
                                   const float* __restrict__ lse, float* __restrict__ dpsum,
-                                  float* __restrict__ lse_log2, float* __restrict__ dq_accum, int sq,
+                                  float* __restrict__ neg_lse_log2, float* __restrict__ dq_accum, int sq,
                                   int sq_rounded, int h);
 __global__ void wf_convert_kernel(const float* __restrict__ accum, __nv_bfloat16* __restrict__ out, float scale,
                                   int s, int s_rounded, int h);

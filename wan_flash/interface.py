@@ -173,7 +173,7 @@ def _bwd_impl(q, k, v, o, lse, do, marks=None):
     sq_rounded, nsplit = plan["sq_rounded"], plan["nsplit"]
     dev = q.device
     dpsum = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
-    lse_log2 = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
+    neg_lse_log2 = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
     dq_accum = torch.empty(b, h, sq_rounded * d, device=dev, dtype=torch.float32)
     if nsplit > 1:
         # split-M: dK/dV accumulate in fp32 (must start zeroed)
@@ -188,10 +188,10 @@ def _bwd_impl(q, k, v, o, lse, do, marks=None):
     cfg = _lib.BwdCfg(nsplit)
     with torch.cuda.device(dev):
         _mark(marks, "bwd_pre")
-        _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(lse_log2), _ptr(dq_accum),
+        _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(neg_lse_log2), _ptr(dq_accum),
                                 b, sq, sq_rounded, h, stream))
         _mark(marks, "bwd_main")
-        _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse_log2), _ptr(dpsum),
+        _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(neg_lse_log2), _ptr(dpsum),
                                  _ptr(dq_accum), _ptr(main_dk), _ptr(main_dv), b, sq, skv, h,
                                  ctypes.byref(cfg), stream))
         _mark(marks, "bwd_convert")
