@@ -20,7 +20,9 @@
 //   P_t (bf16, 64 columns) overwrites the first half of S_t once S_t is read.
 //
 //   MMA order per KV block j:  PV0(j-1) S0(j) PV1(j-1) S1(j)  -- softmax of
-//   tile 0 overlaps the tensor work of tile 1 and vice versa.  The tensor
+//   tile 0 overlaps the tensor work of tile 1 and vice versa.  P_t is
+//   produced in two key halves with their own barriers, so PV_t starts on
+//   keys 0-63 while the softmax still exponentiates keys 64-127.  The tensor
 //   pipe executes tcgen05.mma in issue order, so S_t(j) never overwrites
 //   P_t(j-1) before PV_t(j-1) has read it, and the commit that signals
 //   "S_t(j) ready" also covers PV_t(j-1) -- O_t is final for block j-1 when
@@ -46,8 +48,8 @@ constexpr int kBarQFull = 0;
 constexpr int kBarKvFull = 1;                    // + slot
 constexpr int kBarKvEmpty = kBarKvFull + kKvSlots;
 constexpr int kBarSFull = kBarKvEmpty + kKvSlots;  // + tile
-constexpr int kBarPFull = kBarSFull + 2;
-constexpr int kBarOFull = kBarPFull + 2;
+constexpr int kBarPFull = kBarSFull + 2;      // + 2 * tile + half (keys 0-63 / 64-127)
+constexpr int kBarOFull = kBarPFull + 4;
 constexpr int kBarDrain = kBarOFull + 2;
 constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kOffTmemHolder = kOffBar + kNumBars * 8;
@@ -61,37 +63,28 @@ size_t fwd_smem_bytes() { return fwd::kSmemBytes; }
 // role ids recorded on a wait timeout
 enum : uint32_t { kRoleSoftmax0 = 1, kRoleSoftmax1 = 2, kRoleMma = 3, kRoleLoad = 4 };
 
-// Exponentials of one 128-column block of scores for this thread's row:
-// P = 2^(s * scale_log2 - m) stored to TMEM as bf16 pairs (chunk by chunk,
-// over the already-read S columns), the fp32 row sum returned in `sum_out`
-// and, with kWithMax, the block's raw row max in `max_out`.  Packed f32x2
-// math and a 3-input max keep the instruction count low: the softmax warps
-// share their SMSPs with the MMA-issuing warp, whose issue rate sets the
-// tensor pipe's.  kFwdPolyEvery > 0 routes one pair in kFwdPolyEvery through the
-// FMA-pipe polynomial exp2 instead of MUFU (off by default: on B200 it costs
-// more issue slots than the MUFU time it saves here).
+// Exponentials of half a 128-column block (two 32-column chunks starting at
+// chunk c0) for this thread's row: P = 2^(s * scale_log2 - m) is stored to
+// TMEM as bf16 pairs over the already-read S columns and the fp32 partial
+// row sum is returned.  Packed f32x2 math keeps the instruction count low:
+// the softmax warps share their SMSPs with the MMA-issuing warp, whose issue
+// rate sets the tensor pipe's.  kFwdPolyEvery > 0 routes one pair in
+// kFwdPolyEvery through the FMA-pipe polynomial exp2 instead of MUFU (off by
+// default: on B200 it costs more issue slots than the MUFU time it saves).
 constexpr int kFwdPolyEvery = 0;
 
-template <bool kWithMax>
-__device__ __forceinline__ void fwd_exp_block(const uint32_t (&s)[4][32], uint32_t tS, float sl2, float neg_m,
-                                              float& sum_out, float& max_out) {
-  const uint64_t sl2x2 = f2_pack(sl2, sl2);
-  const uint64_t negx2 = f2_pack(neg_m, neg_m);
+__device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0, uint32_t tS, uint64_t sl2x2,
+                                              uint64_t negx2) {
   uint64_t acc[4];
-  float mx[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    acc[i] = f2_pack(0.f, 0.f);
-    mx[i] = -INFINITY;
-  }
+  for (int i = 0; i < 4; ++i) acc[i] = f2_pack(0.f, 0.f);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int cc = 0; cc < 2; ++cc) {
+    const int c = c0 + cc;
     uint32_t pk[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float s0 = __uint_as_float(s[c][2 * i]), s1 = __uint_as_float(s[c][2 * i + 1]);
-      if (kWithMax) mx[i & 3] = fmax3(mx[i & 3], s0, s1);
-      const uint64_t x = f2_fma(f2_pack(s0, s1), sl2x2, negx2);
+      const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2, negx2);
       const uint64_t pp =
           (kFwdPolyEvery > 0 && (i % kFwdPolyEvery) == kFwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
       acc[i & 3] = f2_add(acc[i & 3], pp);
@@ -103,8 +96,7 @@ __device__ __forceinline__ void fwd_exp_block(const uint32_t (&s)[4][32], uint32
   }
   float a0, a1;
   f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), a0, a1);
-  sum_out = a0 + a1;
-  max_out = kWithMax ? fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) : 0.f;
+  return a0 + a1;
 }
 
 __global__ void __launch_bounds__(fwd::kThreads, 1)
@@ -134,7 +126,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
-      mbar_init(bar(kBarPFull + t), 128);
+      mbar_init(bar(kBarPFull + 2 * t), 128);
+      mbar_init(bar(kBarPFull + 2 * t + 1), 128);
       mbar_init(bar(kBarOFull + t), 1);
     }
     mbar_init(bar(kBarDrain), 1);
@@ -199,6 +192,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       const uint32_t sKV = sbase + kOffKV;
       bool ok = mbar_wait(bar(kBarQFull), 0, abort_flag, kRoleMma, 0);
       tc_fence_after();
+      int pv_phase[2] = {0, 0};
       auto issue_s = [&](int t, int slot_k) {
         const uint32_t d = tmem + (uint32_t)(t * 128);
         const uint64_t a0 = sdesc(sQ + t * kTileBytes, 16, 1024);
@@ -209,13 +203,26 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
           mma_ss(d, desc_add(a0, off), desc_add(b0, off), idesc_qk, ks > 0);
         }
       };
-      auto issue_pv = [&](int t, int slot_v, bool acc) {
+      // O_t += P_t V over keys [64*half, 64*half + 64) once that half of P_t
+      // has been written (P_t: bf16 pairs in S_t columns [0, 64))
+      auto issue_pv_half = [&](int t, int half, int slot_v, bool acc) -> bool {
+        if (!mbar_wait(bar(kBarPFull + 2 * t + half), (uint32_t)pv_phase[t] & 1, abort_flag, kRoleMma, 20 + 2 * t + half))
+          return false;
+        tc_fence_after();
         const uint32_t d = tmem + 256u + (uint32_t)(t * 128);
-        const uint32_t a = tmem + (uint32_t)(t * 128);  // P_t: bf16 pairs in S_t columns [0, 64)
+        const uint32_t a = tmem + (uint32_t)(t * 128);
         const uint64_t b0 = sdesc(sKV + slot_v * kTileBytes, kBoxBytes, 1024);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
+        for (int kk = 0; kk < 4; ++kk) {
+          const int ks = half * 4 + kk;
           mma_ts(d, a + ks * 8, desc_add(b0, (uint32_t)(ks * 2048)), idesc_pv, (acc || ks > 0) ? 1u : 0u);
+        }
+        return true;
+      };
+      auto issue_pv = [&](int t, int slot_v, bool acc) -> bool {
+        const bool r = issue_pv_half(t, 0, slot_v, acc) && issue_pv_half(t, 1, slot_v, acc);
+        pv_phase[t]++;
+        return r;
       };
       for (int it = 0; it < n_blocks && ok; ++it) {
         const int uk = 2 * it, slot_k = uk % kKvSlots;
@@ -229,10 +236,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
               ok = mbar_wait(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
               if (!ok) break;
             }
-            ok = mbar_wait(bar(kBarPFull + t), (it - 1) & 1, abort_flag, kRoleMma, 20 + t);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(t, slot_v, it - 1 > 0);
+            if (!(ok = issue_pv(t, slot_v, it - 1 > 0))) break;
             if (t == 1) mma_commit(bar(kBarKvEmpty + slot_v));
           }
           issue_s(t, slot_k);
@@ -244,10 +248,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         const int uv = 2 * (n_blocks - 1) + 1, slot_v = uv % kKvSlots;
         ok = mbar_wait(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
         for (int t = 0; t < 2 && ok; ++t) {
-          ok = mbar_wait(bar(kBarPFull + t), (n_blocks - 1) & 1, abort_flag, kRoleMma, 20 + t);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(t, slot_v, n_blocks - 1 > 0);
+          if (!(ok = issue_pv(t, slot_v, n_blocks - 1 > 0))) break;
           mma_commit(bar(kBarOFull + t));
         }
         if (ok) mma_commit(bar(kBarKvEmpty + slot_v));
@@ -281,31 +282,26 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
-      float bsum, bmax;
-      if (it == 0) {
-        // first (ragged tail) block: mask, reduce the row max, then exponentiate
-        if (tail_valid < 128) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
-        }
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (it == 0 && tail_valid < 128) {
+        // first (ragged tail) block: keys past skv do not exist
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            mx[i & 3] = fmax3(mx[i & 3], __uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1]));
-        m_s = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
-        fwd_exp_block<false>(s, tS, sl2, -m_s, bsum, bmax);
-        l = bsum;
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          mx[i & 3] = fmax3(mx[i & 3], __uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1]));
+      const float mnew_s = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+      if (it == 0) {
+        m_s = mnew_s;
       } else {
-        // speculative: exponentiate against the running reference max while
-        // reducing this block's max; redo only if the max moved past the
-        // rescale threshold (rare after the first blocks)
-        fwd_exp_block<true>(s, tS, sl2, -m_s, bsum, bmax);
-        const float mnew_s = bmax * sl2;
+        // move the reference max only when the row max grew past the rescale
+        // threshold (exact by max-shift invariance; rare after a few blocks)
         const bool need = mnew_s - m_s > thr;
         if (__any_sync(0xffffffffu, need)) {
           const float factor = need ? ex2_approx(m_s - mnew_s) : 1.f;
@@ -324,14 +320,20 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
             for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
             tmem_st16(tO + c * 16, o);
           }
-          tmem_wait_st();
-          fwd_exp_block<false>(s, tS, sl2, -m_s, bsum, bmax);
         }
-        l += bsum;
       }
+      // P in two halves: the PV MMA on keys 0-63 starts while keys 64-127
+      // are still being exponentiated
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), negx2 = f2_pack(-m_s, -m_s);
+      float bsum = fwd_exp_half(s, 0, tS, sl2x2, negx2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull + t));
+      mbar_arrive(bar(kBarPFull + 2 * t));
+      bsum += fwd_exp_half(s, 2, tS, sl2x2, negx2);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(kBarPFull + 2 * t + 1));
+      l += bsum;
     }
     // ----------------------------------------------------------- epilogue
     if (ok) ok = mbar_wait(bar(kBarOFull + t), 0, abort_flag, role, 40 + t);
