@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         tma_load_4d(sbase + kOffK + x * kBoxBytes, &tm_k, bar(kBarKvFull), x * 64, n0, h, b);
         tma_load_4d(sbase + kOffV + x * kBoxBytes, &tm_v, bar(kBarKvFull), x * 64, n0, h, b);
       }
-      int issued[2] = {0, 0};
+      int issued0 = 0, issued1 = 0;  // completed-use counts per stage (for the abort drain)
       for (int u = 0; u < cnt; ++u) {
         const int st = u & 1, use = u >> 1;
         if (use > 0 && !mbar_wait(bar(kBarQdoEmpty + st), (use - 1) & 1, abort_flag, kRoleBwdLoad, 3 + st)) break;
@@ -167,12 +167,12 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         const size_t row0 = bh * (size_t)p.sq_rounded + (size_t)m * 128;
         bulk_load(sbase + kOffLse + st * 512, p.neg_lse_log2 + row0, 512, full);
         bulk_load(sbase + kOffD + st * 512, p.dpsum + row0, 512, full);
-        issued[st] = use + 1;
+        if (st) issued1 = use + 1; else issued0 = use + 1;
       }
       if (*abort_flag) {
         mbar_wait_drain(bar(kBarKvFull), 0);
-        for (int st = 0; st < 2; ++st)
-          if (issued[st] > 0) mbar_wait_drain(bar(kBarQdoFull + st), (issued[st] - 1) & 1);
+        if (issued0 > 0) mbar_wait_drain(bar(kBarQdoFull + 0), (issued0 - 1) & 1);
+        if (issued1 > 0) mbar_wait_drain(bar(kBarQdoFull + 1), (issued1 - 1) & 1);
       }
     }
   } else if (warp == 12) {
