@@ -106,6 +106,25 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
  */
 int wf_bwd_convert(const float* accum, void* out, float scale, int b, int s, int h, void* stream);
 
+/*
+ * Backward without caller workspaces: the whole chain of wf_bwd_pre,
+ * wf_bwd_main (nsplit = 1) and wf_bwd_convert, with the three fp32
+ * workspaces taken from a 64 MiB array compiled into this library.  No
+ * counterpart in the reference (its driver always allocates workspaces with
+ * torch, wan_flash/interface.py:137-149); it exists for callers that can pass
+ * tensors but cannot allocate device memory at call time -- a plugin host
+ * that owns every device allocation, or a latency-critical caller that cannot
+ * afford cudaMalloc's implicit synchronisation.  It never allocates.
+ *   q, k, v, o, dO, dq, dk, dv: as wan_flash_bwd; lse (b, h, sq) natural log.
+ *   Limit: b * h * ceil(sq/128)*128 <= 129,024 query rows (520 bytes of
+ *   scratch each); larger calls return WF_ERR_UNSUPPORTED before any work.
+ *   All calls share the one array: calls that overlap on the GPU race.
+ *   The first call on a device looks up the array's address; make it before
+ *   any stream capture.
+ */
+int wf_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse, const void* dO,
+                   void* dq, void* dk, void* dv, int b, int sq, int skv, int h, void* stream);
+
 /* Message for the last failed call on this thread (empty if none). */
 int wf_last_error(char* buf, int len);
 

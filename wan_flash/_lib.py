@@ -28,7 +28,7 @@ STATUS_NAMES = {
 }
 
 EXPORTS = (
-    "wf_fwd", "wf_bwd_pre", "wf_bwd_main", "wf_bwd_convert", "wf_last_error",
+    "wf_fwd", "wf_bwd_pre", "wf_bwd_main", "wf_bwd_convert", "wf_bwd_noalloc", "wf_last_error",
     "wf_device_status", "wf_set_wait_limit_ns", "wf_num_sms", "wf_version",
 )
 
@@ -54,6 +54,7 @@ def _declare(lib):
     lib.wf_bwd_pre.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]
     lib.wf_bwd_main.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, ctypes.POINTER(BwdCfg), vp]
     lib.wf_bwd_convert.argtypes = [vp, vp, f, i, i, i, vp]
+    lib.wf_bwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp]
     lib.wf_last_error.argtypes = [ctypes.c_char_p, i]
     lib.wf_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.wf_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]

@@ -5,3 +5,4 @@
 #include "wf_fwd.cu"
 #include "wf_bwd.cu"
 #include "wf_aux.cu"
+#include "wf_noalloc.cu"
