@@ -52,6 +52,10 @@ CONFIGS = {
     "c4": ("self", 1, 75600, 75600, 40, 3, "Wan2.1-14B 720p self-attention fwd+bwd, head-sharded (b=1, s=75600, h=40)"),
 }
 METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/4/8-GPU"
+# DRAM bytes (read + write) per launch per head, from one ncu capture of the
+# C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd_c2_h4.md);
+# traffic grows with the number of heads, so it is scaled by the run's heads.
+DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 317.79e6 / 4, ("c2", "fwd"): 116.37e6 / 4}
 NOMINAL_BF16_TFLOPS = 2250.0
 
 
@@ -389,7 +393,10 @@ def main():
             "kernel_ms": kern_ms,
             "roofline": {
                 "kernel": dominant, "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "traffic": (DRAM_BYTES_PER_HEAD[(args.config, dominant)] * h
+                            if (args.config, dominant) in DRAM_BYTES_PER_HEAD else None),
+                "traffic_unit": "bytes per launch (ncu capture at 4 heads, scaled by heads)",
                 "peak_source": f"{peaks['source']} burst bf16 (MEASURED_PEAKS.json)" if peaks["source"] == "measured"
                 else "fallback 1.59 PFLOP/s",
             },
