@@ -16,18 +16,24 @@
 //   warps 0-3   elementwise WG A: thread = one KV row, query columns [0, 64)
 //   warps 4-7   elementwise WG B: thread = one KV row, query columns [64, 128)
 //   warps 8-11  dQ WG: thread = one query row; drains dQ from TMEM and
-//               reduces it into dq_accum with vector fp32 reductions
+//               reduces it into dq_accum with bulk async reductions staged
+//               through a dedicated buffer
 //   warp  12    tcgen05.mma issuer + TMEM owner
-//   warp  13    TMA producer (K/V once; Q, dO, -lse*log2(e), D double-buffered)
+//   warp  13    TMA producer (K/V once; Q, -lse*log2(e), D double-buffered;
+//               dO single-buffered, refilled between dV(u) and dP(u+1))
 //   warps 14-15 idle (complete warpgroup 3 so it can give registers back)
 //
 //   TMEM (512 columns): S^T [0,128) -- P^T (bf16) overwrites [0,32) (WG A)
 //   and [64,96) (WG B), each inside the columns that WG has already read;
-//   dP^T [128,256) -- dQ reuses it once dS has been formed; dV [256,384);
-//   dK [384,512).  dS^T goes to shared memory (128B-swizzled, [kv][q]): the
-//   dK MMA reads it K-major and the dQ MMA reads the same bytes MN-major.
+//   dP^T [128,256) -- dS^T (bf16) overwrites it the same way as the A operand
+//   of the dK MMA, and dQ reuses all of it once dK has read dS^T; dV
+//   [256,384); dK [384,512).  dS^T also goes to shared memory (128B-swizzled,
+//   [kv][q]), read MN-major by the dQ MMA.
+//   A separate 32 KB buffer stages dQ for the bulk reductions.
 //
 //   MMA order for query block u:  dV(u)  S(u+1)  dK(u)  dQ(u)  dP(u+1)
+//   (dV and dK take their A operand from TMEM; S, dP and dQ read both from
+//   shared memory)
 //   S(u+1) only needs dV(u) to have read P^T(u) (in-order tensor pipe), so
 //   the next exponentials start while dK/dQ of this block run; dP(u+1)
 //   waits for the dQ warpgroup to have read dQ(u) out of the dP columns.
@@ -48,24 +54,29 @@ constexpr uint32_t kTileBytes = 2 * kBoxBytes;  // 128 rows x 128 bf16
 constexpr uint32_t kOffK = 0;
 constexpr uint32_t kOffV = kOffK + kTileBytes;
 constexpr uint32_t kOffQ = kOffV + kTileBytes;       // 2 stages
-constexpr uint32_t kOffdO = kOffQ + 2 * kTileBytes;  // 2 stages
-constexpr uint32_t kOffdS = kOffdO + 2 * kTileBytes;
-constexpr uint32_t kOffLse = kOffdS + kTileBytes;    // 2 stages x 128 fp32 (-lse * log2 e)
+constexpr uint32_t kOffdO = kOffQ + 2 * kTileBytes;  // 1 stage (free after dV, refilled before dP)
+constexpr uint32_t kOffdS = kOffdO + kTileBytes;
+constexpr uint32_t kOffX = kOffdS + kTileBytes;      // dQ staging for the bulk reductions (32 KB)
+constexpr uint32_t kOffLse = kOffX + kTileBytes;     // 2 stages x 128 fp32 (-lse * log2 e)
 constexpr uint32_t kOffD = kOffLse + 2 * 512;        // 2 stages x 128 fp32
 constexpr uint32_t kOffBar = kOffD + 2 * 512;
 constexpr int kBarKvFull = 0;
-constexpr int kBarQdoFull = 1;   // + stage
-constexpr int kBarQdoEmpty = 3;  // + stage
-constexpr int kBarSFull = 5;
-constexpr int kBarDpFull = 6;
-constexpr int kBarPReady = 7;
-constexpr int kBarDsReady = 8;
-constexpr int kBarDsEmpty = 9;
-constexpr int kBarDqFull = 10;
-constexpr int kBarDqDrained = 11;
-constexpr int kBarDkvFull = 12;
-constexpr int kBarDrain = 13;
-constexpr int kNumBars = 14;
+constexpr int kBarQFull = 1;     // + stage (with -lse*log2e and D of the block)
+constexpr int kBarQEmpty = 3;    // + stage
+constexpr int kBarDoFull = 5;
+constexpr int kBarDoEmpty = 6;
+constexpr int kBarSFull = 7;
+constexpr int kBarDpFull = 8;
+constexpr int kBarPReady = 9;
+constexpr int kBarDsReady = 10;
+constexpr int kBarDsEmpty = 11;
+constexpr int kBarDqFull = 12;
+constexpr int kBarDqDrained = 13;
+constexpr int kBarDkvFull = 14;
+constexpr int kBarDrain = 15;
+constexpr int kBarXchgFull = 16;   // the dQ warpgroup has written a half-tile into the staging buffer
+constexpr int kBarXchgDone = 17;   // the staging buffer is free again (previous bulk read done)
+constexpr int kNumBars = 18;
 constexpr uint32_t kOffTmemHolder = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemHolder + 4;
 constexpr uint32_t kSmemUsed = kOffAbort + 4;
@@ -124,7 +135,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       const bool ew = (i == kBarPReady || i == kBarDsReady);
-      mbar_init(bar(i), ew ? 256u : (i == kBarDqDrained ? 128u : 1u));
+      const uint32_t count = ew ? 256u : (i == kBarDqDrained || i == kBarXchgDone || i == kBarXchgFull) ? 128u : 1u;
+      mbar_init(bar(i), count);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -153,26 +165,31 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         tma_load_4d(sbase + kOffK + x * kBoxBytes, &tm_k, bar(kBarKvFull), x * 64, n0, h, b);
         tma_load_4d(sbase + kOffV + x * kBoxBytes, &tm_v, bar(kBarKvFull), x * 64, n0, h, b);
       }
-      int issued0 = 0, issued1 = 0;  // completed-use counts per stage (for the abort drain)
+      int issued0 = 0, issued1 = 0, issued_do = 0;  // completed uses per buffer (for the abort drain)
       for (int u = 0; u < cnt; ++u) {
         const int st = u & 1, use = u >> 1;
-        if (use > 0 && !mbar_wait(bar(kBarQdoEmpty + st), (use - 1) & 1, abort_flag, kRoleBwdLoad, 3 + st)) break;
         const int m = m_begin + u;
-        const uint32_t full = bar(kBarQdoFull + st);
-        mbar_expect_tx(full, 2 * kTileBytes + 1024);
-        for (int x = 0; x < 2; ++x) {
-          tma_load_4d(sbase + kOffQ + st * kTileBytes + x * kBoxBytes, &tm_q, full, x * 64, m * 128, h, b);
-          tma_load_4d(sbase + kOffdO + st * kTileBytes + x * kBoxBytes, &tm_do, full, x * 64, m * 128, h, b);
-        }
+        if (use > 0 && !mbar_wait(bar(kBarQEmpty + st), (use - 1) & 1, abort_flag, kRoleBwdLoad, 3 + st)) break;
+        const uint32_t qfull = bar(kBarQFull + st);
+        mbar_expect_tx(qfull, kTileBytes + 1024);
+        for (int x = 0; x < 2; ++x)
+          tma_load_4d(sbase + kOffQ + st * kTileBytes + x * kBoxBytes, &tm_q, qfull, x * 64, m * 128, h, b);
         const size_t row0 = bh * (size_t)p.sq_rounded + (size_t)m * 128;
-        bulk_load(sbase + kOffLse + st * 512, p.neg_lse_log2 + row0, 512, full);
-        bulk_load(sbase + kOffD + st * 512, p.dpsum + row0, 512, full);
+        bulk_load(sbase + kOffLse + st * 512, p.neg_lse_log2 + row0, 512, qfull);
+        bulk_load(sbase + kOffD + st * 512, p.dpsum + row0, 512, qfull);
         if (st) issued1 = use + 1; else issued0 = use + 1;
+        // dO has one buffer: refill it once dV of the previous block has read it
+        if (u > 0 && !mbar_wait(bar(kBarDoEmpty), (u - 1) & 1, abort_flag, kRoleBwdLoad, 6)) break;
+        mbar_expect_tx(bar(kBarDoFull), kTileBytes);
+        for (int x = 0; x < 2; ++x)
+          tma_load_4d(sbase + kOffdO + x * kBoxBytes, &tm_do, bar(kBarDoFull), x * 64, m * 128, h, b);
+        issued_do = u + 1;
       }
       if (*abort_flag) {
         mbar_wait_drain(bar(kBarKvFull), 0);
-        if (issued0 > 0) mbar_wait_drain(bar(kBarQdoFull + 0), (issued0 - 1) & 1);
-        if (issued1 > 0) mbar_wait_drain(bar(kBarQdoFull + 1), (issued1 - 1) & 1);
+        if (issued0 > 0) mbar_wait_drain(bar(kBarQFull + 0), (issued0 - 1) & 1);
+        if (issued1 > 0) mbar_wait_drain(bar(kBarQFull + 1), (issued1 - 1) & 1);
+        if (issued_do > 0) mbar_wait_drain(bar(kBarDoFull), (issued_do - 1) & 1);
       }
     }
   } else if (warp == 12) {
@@ -189,7 +206,6 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       // the offset to the encoded start-address field).
       const uint64_t dK_k = sdesc(sbase + kOffK, 16, 1024);
       const uint64_t dV_k = sdesc(sbase + kOffV, 16, 1024);
-      const uint64_t dS_k = sdesc(sbase + kOffdS, 16, 1024);
       const uint64_t dK_mn = sdesc(sbase + kOffK, kBoxBytes, 1024);
       const uint64_t dS_mn = sdesc(sbase + kOffdS, kBoxBytes, 1024);
       auto koff = [](int ks) -> uint32_t { return (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32); };
@@ -200,17 +216,19 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         for (int ks = 0; ks < 8; ++ks) mma_ss(tS, desc_add(dK_k, koff(ks)), desc_add(q_k, koff(ks)), id_kk, ks > 0);
         mma_commit(bar(kBarSFull));
       };
-      auto issue_dp = [&](int st) {  // dP^T = V dO^T
-        const uint64_t do_k = sdesc(sbase + kOffdO + st * kTileBytes, 16, 1024);
+      const uint64_t do_k = sdesc(sbase + kOffdO, 16, 1024);
+      const uint64_t do_mn = sdesc(sbase + kOffdO, kBoxBytes, 1024);
+      auto issue_dp = [&]() {  // dP^T = V dO^T
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, desc_add(dV_k, koff(ks)), desc_add(do_k, koff(ks)), id_kk, ks > 0);
         mma_commit(bar(kBarDpFull));
       };
       bool ok = mbar_wait(bar(kBarKvFull), 0, abort_flag, kRoleBwdMma, 0) &&
-                mbar_wait(bar(kBarQdoFull + 0), 0, abort_flag, kRoleBwdMma, 1);
+                mbar_wait(bar(kBarQFull + 0), 0, abort_flag, kRoleBwdMma, 1) &&
+                mbar_wait(bar(kBarDoFull), 0, abort_flag, kRoleBwdMma, 5);
       if (ok) {
         tc_fence_after();
-        issue_dp(0);
+        issue_dp();
         issue_s(0);
       }
       for (int u = 0; u < cnt && ok; ++u) {
@@ -218,35 +236,36 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         // dV += P^T dO   (P^T from TMEM: query 0-63 in columns [0,32), 64-127 in [64,96))
         if (!(ok = mbar_wait(bar(kBarPReady), u & 1, abort_flag, kRoleBwdMma, 7))) break;
         tc_fence_after();
-        const uint64_t do_mn = sdesc(sbase + kOffdO + st * kTileBytes, kBoxBytes, 1024);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           mma_ts(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(do_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(bar(kBarDoEmpty));  // dO(u) is read by dP(u) and dV(u) only
         // S^T(u+1): the S columns are free once dV(u) has read P^T(u)
         if (u + 1 < cnt) {
-          if (!(ok = mbar_wait(bar(kBarQdoFull + ((u + 1) & 1)), ((u + 1) >> 1) & 1, abort_flag, kRoleBwdMma, 1)))
+          if (!(ok = mbar_wait(bar(kBarQFull + ((u + 1) & 1)), ((u + 1) >> 1) & 1, abort_flag, kRoleBwdMma, 1)))
             break;
           tc_fence_after();
           issue_s((u + 1) & 1);
         }
-        // dK += dS^T Q   (dS^T from smem, K-major)
+        // dK += dS^T Q   (dS^T from TMEM: query 0-63 in dP columns [0,32), 64-127 in [64,96))
         if (!(ok = mbar_wait(bar(kBarDsReady), u & 1, abort_flag, kRoleBwdMma, 8))) break;
         tc_fence_after();
         const uint64_t q_mn = sdesc(sbase + kOffQ + st * kTileBytes, kBoxBytes, 1024);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdK, desc_add(dS_k, koff(ks)), desc_add(q_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(bar(kBarQdoEmpty + st));
+          mma_ts(tdK, tdP + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(q_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(bar(kBarQEmpty + st));
         // dQ_blk = dS K   (same dS bytes read MN-major) into the dP^T columns
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, desc_add(dS_mn, moff(ks)), desc_add(dK_mn, moff(ks)), id_mm, ks > 0);
         mma_commit(bar(kBarDqFull));
         mma_commit(bar(kBarDsEmpty));
-        // dP^T(u+1) once dQ(u) has been read out of those columns
+        // dP^T(u+1) once dQ(u) has been read out of those columns and dO(u+1) is in
         if (u + 1 < cnt) {
           if (!(ok = mbar_wait(bar(kBarDqDrained), u & 1, abort_flag, kRoleBwdMma, 11))) break;
+          if (!(ok = mbar_wait(bar(kBarDoFull), (u + 1) & 1, abort_flag, kRoleBwdMma, 5))) break;
           tc_fence_after();
-          issue_dp((u + 1) & 1);
+          issue_dp();
         }
       }
       if (ok) mma_commit(bar(kBarDkvFull));
@@ -274,7 +293,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       if (!(ok = mbar_wait(bar(kBarSFull), u & 1, abort_flag, kRoleEw, 5))) break;
       // -lse*log2(e) / D of this block arrived with Q/dO (already complete; this
       // wait makes the bulk-copied bytes visible to these threads)
-      if (!(ok = mbar_wait(bar(kBarQdoFull + st), (u >> 1) & 1, abort_flag, kRoleEw, 1))) break;
+      if (!(ok = mbar_wait(bar(kBarQFull + st), (u >> 1) & 1, abort_flag, kRoleEw, 1))) break;
       tc_fence_after();
       uint32_t s[2][32];
       tmem_ld32(tS, s[0]);
@@ -336,7 +355,11 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
             pk[i] = kv_valid ? pack_bf16(d0, d1) : 0u;
           }
         }
-        // row r of dS^T, query columns [64*half + 32c, +32): 4 chunks of 16 B
+        // dS^T as the A operand of the dK MMA: bf16 pairs over this warpgroup's
+        // (already read) dP^T columns
+        tmem_st16(tdP + c * 16, pk);
+        // row r of dS^T in shared memory for the dQ MMA, query columns
+        // [64*half + 32c, +32): 4 chunks of 16 B
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           const uint32_t off = sw128_offset((uint32_t)r, (uint32_t)(c * 4 + v));
@@ -344,6 +367,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         }
       }
       fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(bar(kBarDsReady));
     }
     // ----------------------------------------------------------- epilogue
@@ -385,9 +410,19 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   } else {
     regs_inc<kRegsDq>();
     // ------------------------------------------------------- dQ warpgroup
+    // dQ(u) leaves TMEM into registers (then the dP^T columns are free for
+    // dP(u+1)), goes through a dedicated 32 KB staging buffer in two halves
+    // and is reduced into dq_accum by one bulk cp.reduce.async per half (the
+    // accumulator's 128-row tile is [32 groups of 4 columns][128 rows][4], so
+    // a half is 32 contiguous KB).  The bulk engine, not the per-SMSP
+    // load/store pipe, carries the reduction, which keeps that pipe free for
+    // the TMEM, shared-memory and mbarrier traffic of the other warps.
     const int wq = warp & 3;
     const int r = wq * 32 + lane;  // query row within the block
     const uint32_t tQ = tmem + ((uint32_t)(wq * 32) << 16) + 128u;  // dQ lives in the dP^T columns
+    const uint32_t sx = sbase + kOffX;
+    uint8_t* xb = smem + kOffX;
+    const bool leader = (threadIdx.x == 256);
     for (int u = 0; u < cnt; ++u) {
       if (!mbar_wait(bar(kBarDqFull), u & 1, abort_flag, kRoleDq, 10)) break;
       tc_fence_after();
@@ -399,15 +434,31 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       for (int c = 0; c < 4; ++c) reg_fence32(q[c]);
       tc_fence_before();
       mbar_arrive(bar(kBarDqDrained));
-      float* tile = p.dq_accum + (bh * (size_t)p.m_blocks + (m_begin + u)) * 16384 + (size_t)r * 4;
+      float* tile = p.dq_accum + (bh * (size_t)p.m_blocks + (m_begin + u)) * 16384;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int half = 0; half < 2; ++half) {
+        // the staging buffer is free once the previous bulk reduction has read it
+        if (leader) bulk_wait_read_all();
+        mbar_arrive(bar(kBarXchgDone));
+        if (!mbar_wait(bar(kBarXchgDone), (2 * u + half) & 1, abort_flag, kRoleDq, 16)) break;
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          red_add_v4(tile + (size_t)(c * 8 + g) * 512, __uint_as_float(q[c][4 * g + 0]),
-                     __uint_as_float(q[c][4 * g + 1]), __uint_as_float(q[c][4 * g + 2]),
-                     __uint_as_float(q[c][4 * g + 3]));
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            *reinterpret_cast<uint4*>(xb + ((cc * 8 + g) * 128 + r) * 16) =
+                make_uint4(q[2 * half + cc][4 * g + 0], q[2 * half + cc][4 * g + 1], q[2 * half + cc][4 * g + 2],
+                           q[2 * half + cc][4 * g + 3]);
+        fence_proxy_async_smem();
+        mbar_arrive(bar(kBarXchgFull));
+        if (leader) {
+          if (!mbar_wait(bar(kBarXchgFull), (2 * u + half) & 1, abort_flag, kRoleDq, 15)) break;
+          bulk_reduce_add_f32(tile + half * 8192, sx, 32768);
+          bulk_commit_group();
+        }
+      }
+      if (*abort_flag) break;
     }
+    if (leader) bulk_wait_all();
   }
 
   __syncwarp();

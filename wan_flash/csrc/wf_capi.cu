@@ -251,9 +251,12 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
       (rc = make_bshd_map(&mv, v, b, skv, h)) || (rc = make_bshd_map(&mdo, dO, b, sq, h)))
     return rc;
   const int splits = (p.m_blocks + p.m_chunk - 1) / p.m_chunk;  // every split owns >= 1 m-block
+  p.n_blocks_padded = p.n_blocks;
   dim3 grid(p.n_blocks * splits, h, b);
   wf_bwd_main_kernel<<<grid, kBwdThreads, bwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mdo,
                                                                                                        p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_main launch");
   return launch_check("wf_bwd_main launch");
 }
 

@@ -26,6 +26,7 @@ struct BwdParams {
   void* dv;
   int sq, skv, h;
   int sq_rounded, m_blocks, n_blocks, skv_rounded;
+  int n_blocks_padded;     // n_blocks rounded up to the 2-CTA cluster size
   int accum_dkv;           // 1: dk/dv are fp32 tiled accumulators (split-M)
   int m_chunk;             // split-M: m-blocks per CTA
   float scale;             // 1/sqrt(128)
