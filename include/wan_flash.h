@@ -139,6 +139,16 @@ int wf_device_status(unsigned int* info);
 /* Set the device-side wait limit in nanoseconds (default 2^31). */
 int wf_set_wait_limit_ns(unsigned long long ns);
 
+/*
+ * Self-test of device-side failure detection: launches one thread that waits
+ * on an mbarrier nothing arrives on, with the wait limit set to `limit_ns`,
+ * synchronises, and returns what wf_device_status reports (WF_ERR_WAIT_TIMEOUT
+ * when the machinery works; `info` as in wf_device_status).  The previous
+ * limit is restored.  No reference counterpart (the reference has no failure
+ * detection); nothing is in flight, so the expiry cannot harm the context.
+ */
+int wf_selftest_wait_timeout(unsigned long long limit_ns, unsigned int* info);
+
 /* Number of SMs of the current device (0 on error). */
 int wf_num_sms(void);
 

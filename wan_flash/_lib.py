@@ -29,7 +29,7 @@ STATUS_NAMES = {
 
 EXPORTS = (
     "wf_fwd", "wf_bwd_pre", "wf_bwd_main", "wf_bwd_convert", "wf_bwd_noalloc", "wf_last_error",
-    "wf_device_status", "wf_set_wait_limit_ns", "wf_num_sms", "wf_version",
+    "wf_device_status", "wf_set_wait_limit_ns", "wf_selftest_wait_timeout", "wf_num_sms", "wf_version",
 )
 
 
@@ -58,6 +58,7 @@ def _declare(lib):
     lib.wf_last_error.argtypes = [ctypes.c_char_p, i]
     lib.wf_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.wf_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
+    lib.wf_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint)]
     for name in EXPORTS:
         getattr(lib, name).restype = ctypes.c_int
     del fp

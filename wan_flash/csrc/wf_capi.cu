@@ -120,6 +120,22 @@ int launch_check(const char* what) {
 }
 
 }  // namespace
+
+// Self-test of the bounded-wait machinery: one thread waits on an mbarrier that
+// nothing arrives on.  No copies or MMAs are in flight, so the expiry path is
+// exercised without any risk to the context.
+__global__ void wf_selftest_wait_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, 99u, 99u);
+}
+
 }  // namespace wf
 
 using namespace wf;
@@ -164,6 +180,21 @@ int wf_device_status(unsigned int* info) {
                 inf[0] >> 16, inf[1], inf[2], inf[3]);
   }
   return WF_OK;
+}
+
+int wf_selftest_wait_timeout(unsigned long long limit_ns, unsigned int* info) {
+  int dev, rc;
+  if ((rc = device_setup(&dev))) return rc;
+  if ((rc = wf_device_status(nullptr))) return rc;  // start from a clean error word
+  unsigned long long old_limit = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&old_limit, g_wait_limit_ns, sizeof(old_limit));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(wait limit)");
+  if ((rc = wf_set_wait_limit_ns(limit_ns))) return rc;
+  wf_selftest_wait_kernel<<<1, 32>>>();
+  e = cudaGetLastError();
+  const int status = (e == cudaSuccess) ? wf_device_status(info) : cuda_fail(e, "selftest launch");
+  const int rc2 = wf_set_wait_limit_ns(old_limit);
+  return status != WF_OK ? status : rc2;
 }
 
 int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int b, int sq, int skv, int h,
