@@ -199,6 +199,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override heads per GPU (small profiling cases)")
+    ap.add_argument("--bwd-cluster-n", type=int, default=0, choices=[0, 1, 2],
+                    help="backward kernel form: 1 = single CTAs, 2 = CTA pairs, 0 = the feature default")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -237,7 +239,10 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from wan_flash import _lib, interface
+    from wan_flash import _lib, features, interface
+
+    if args.bwd_cluster_n:
+        features.set_bwd_overrides(cluster_n=args.bwd_cluster_n)
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -437,6 +442,7 @@ def main():
             "clocks": clk,
             "gpu_launches": launches_per_step * args.steps,
             "bwd_nsplit": plan["nsplit"],
+            "bwd_cluster_n": plan["cluster_n"],
         }
         print(json.dumps(line), flush=True)
     if world > 1:

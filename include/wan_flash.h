@@ -54,9 +54,12 @@ typedef struct wf_fwd_cfg {
 
 /* Backward options (mirror BwdFeatures, wan_flash/features.py:45-70). */
 typedef struct wf_bwd_cfg {
-  int nsplit; /* split-M factor >= 1; with nsplit > 1 dk/dv arguments of
-                 wf_bwd_main are fp32 accumulators (zeroed by the caller) */
-  int reserved[3];
+  int nsplit;    /* split-M factor >= 1; with nsplit > 1 dk/dv arguments of
+                    wf_bwd_main are fp32 accumulators (zeroed by the caller) */
+  int cluster_n; /* 0 = auto, 1 = one CTA per KV block, 2 = CTA pairs over
+                    adjacent KV blocks (cluster of 2, 2-SM tensor-core MMAs;
+                    the reference's cluster_n = 2 without multicast loads) */
+  int reserved[2];
 } wf_bwd_cfg;
 
 /*
@@ -98,8 +101,9 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
 /*
  * Convert a tiled fp32 accumulator to bf16 (b, s, h, 128): out = accum * scale.
  * Tiled layout: for (b, h, 128-row block m) a 128x128 tile stored as
- * [32 column groups of 4][128 rows][4] -- element (row r, col c) of block m
- * at ((b*h_total + h)*m_blocks + m)*16384 + ((c/4)*128 + r)*4 + c%4.
+ * [2 row halves][32 column groups of 4][64 rows][4] -- element (row r, col c)
+ * of block m at ((b*h_total + h)*m_blocks + m)*16384 + (r/64)*8192 +
+ * ((c/4)*64 + r%64)*4 + c%4.
  * Replaces `compiled[2](*post_args, stream)` (dQ) and, under split-M,
  * `compiled[3](...)` (dK, dV) of wan_flash/interface.py:192-195
  * (WanFlashBwdPostprocessSm90, wan_flash/bwd_sm90.py:1140-1308).

@@ -80,6 +80,60 @@ def test_bwd_nsplit(shape, nsplit):
         features.reset()
 
 
+PAIR_SHAPES = [
+    WanShape("self", 1, 2, 1024, 1024),
+    WanShape("self", 1, 2, 960, 960),      # K tail inside the pair's second CTA
+    WanShape("self", 1, 3, 1100, 1300),    # odd KV block count: last pair's second CTA is empty
+    WanShape("cross", 1, 2, 2048, 512),
+    WanShape("cross", 1, 2, 2048, 257),    # one pair, second CTA holds a single key
+    WanShape("self", 2, 3, 700, 520),
+]
+
+
+@pytest.mark.parametrize("shape", PAIR_SHAPES, ids=lambda s: f"{s.name}-{s.b}x{s.h}x{s.sq}x{s.skv}")
+def test_bwd_cta_pair(shape):
+    """cluster_n = 2: CTA pairs with 2-SM MMAs (dQ from the pair's 256 KV rows)."""
+    from wan_flash import features
+
+    features.set_bwd_overrides(cluster_n=2, nsplit=1)
+    try:
+        _run(shape, seed=13)
+    finally:
+        features.reset()
+
+
+@pytest.mark.parametrize("nsplit", [2, 5])
+def test_bwd_cta_pair_nsplit(nsplit):
+    """CTA pairs with split-M (fp32 dK/dV reductions from both CTAs of a pair)."""
+    from wan_flash import features
+
+    features.set_bwd_overrides(cluster_n=2, nsplit=nsplit)
+    try:
+        _run(WanShape("cross", 1, 2, 3000, 385), seed=17)
+    finally:
+        features.reset()
+
+
+def test_bwd_cta_pair_matches_single():
+    """The pair kernel and the single-CTA kernel agree on all three gradients
+    (same bf16 operands; only the fp32 accumulation / reduction order differs)."""
+    from wan_flash import features
+    from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+
+    q, k, v, do = (t.cuda() for t in seeded(1, 1536, 1536, 2, seed=19))
+    o, lse = wan_flash_fwd(q, k, v)
+    try:
+        features.set_bwd_overrides(cluster_n=1, nsplit=1)
+        a = wan_flash_bwd(q, k, v, o, lse, do)
+        features.set_bwd_overrides(cluster_n=2, nsplit=1)
+        b = wan_flash_bwd(q, k, v, o, lse, do)
+    finally:
+        features.reset()
+    for name, x, y in zip(("dq", "dk", "dv"), a, b):
+        rel = ((x.float() - y.float()).norm() / y.float().norm()).item()
+        assert rel < 1e-3, (name, rel)
+
+
 def test_bwd_oracle_o_lse_contract():
     """Our backward consuming the oracle's o/lse (the natural-log LSE drop-in)."""
     from oracle.oracle import oracle_fwd

@@ -38,7 +38,7 @@ class FwdCfg(ctypes.Structure):
 
 
 class BwdCfg(ctypes.Structure):
-    _fields_ = [("nsplit", ctypes.c_int), ("reserved", ctypes.c_int * 3)]
+    _fields_ = [("nsplit", ctypes.c_int), ("cluster_n", ctypes.c_int), ("reserved", ctypes.c_int * 2)]
 
 
 class WanFlashError(RuntimeError):

@@ -8,9 +8,10 @@
 // so pad rows hold -inf and the main kernel needs one fused multiply-add per
 // exponent) and
 // WanFlashBwdPostprocessSm90, wan_flash/bwd_sm90.py:1140-1308.  The
-// accumulator here is stored in 128-row tiles of [32 groups of 4 columns]
-// [128 rows][4] (the order the backward main kernel reduces into), not the
-// reference's WGMMA fragment order.
+// accumulator here is stored in 128-row tiles of [2 row halves][32 groups of
+// 4 columns][64 rows][4] (each 64-row half is one contiguous 32 KB run, the
+// unit the backward main kernels reduce into), not the reference's WGMMA
+// fragment order.
 #include "wf_common.cuh"
 #include "wf_kernels.h"
 
@@ -65,15 +66,12 @@ __global__ void __launch_bounds__(256) wf_bwd_pre_kernel(const __nv_bfloat16* __
       neg_lse_log2[bh * sq_rounded + s] = nl2;
     }
   }
-  // zero rows [row0, row0 + 64) of the tiled dQ accumulator
-  const int m = row0 >> 7, r0 = row0 & 127;
-  float4* tile = reinterpret_cast<float4*>(dq_accum + (bh * (size_t)(sq_rounded >> 7) + m) * 16384);
+  // zero rows [row0, row0 + 64) of the tiled dQ accumulator: one 64-row half,
+  // a contiguous 32 KB run
+  const int m = row0 >> 7, half = (row0 >> 6) & 1;
+  float4* run = reinterpret_cast<float4*>(dq_accum + (bh * (size_t)(sq_rounded >> 7) + m) * 16384 + half * 8192);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int idx = threadIdx.x + i * 256;  // 0..2047 = 32 groups x 64 rows
-    const int g = idx >> 6, rw = idx & 63;
-    tile[g * 128 + r0 + rw] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int i = 0; i < 8; ++i) run[threadIdx.x + i * 256] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // grid (s_rounded / 32, h, b), 256 threads; tile of 32 rows x 128 columns.
@@ -84,8 +82,9 @@ __global__ void __launch_bounds__(256) wf_convert_kernel(const float* __restrict
   const int h = blockIdx.y, b = blockIdx.z;
   const size_t bh = (size_t)b * h_total + h;
   const int row0 = blockIdx.x * 32;
-  const int m = row0 >> 7, r0 = row0 & 127;
-  const float4* src = reinterpret_cast<const float4*>(accum + (bh * (size_t)(s_rounded >> 7) + m) * 16384);
+  const int m = row0 >> 7, half = (row0 >> 6) & 1, r0 = row0 & 63;
+  const float4* src =
+      reinterpret_cast<const float4*>(accum + (bh * (size_t)(s_rounded >> 7) + m) * 16384 + half * 8192);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int idx = threadIdx.x + i * 256;  // 0..1023 = 32 groups x 32 rows
@@ -93,7 +92,7 @@ __global__ void __launch_bounds__(256) wf_convert_kernel(const float* __restrict
     float4 v;
     asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(src + g * 128 + r0 + rw));
+                 : "l"(src + g * 64 + r0 + rw));
     tile[rw][4 * g + 0] = v.x;
     tile[rw][4 * g + 1] = v.y;
     tile[rw][4 * g + 2] = v.z;

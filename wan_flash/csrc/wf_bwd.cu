@@ -398,10 +398,11 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
                            pack_bf16(__uint_as_float(a[8 * v + 6]) * mul, __uint_as_float(a[8 * v + 7]) * mul));
           }
         } else {
-          float* tile = reinterpret_cast<float*>(dst) + (bh * (size_t)p.n_blocks + nb) * 16384 + (size_t)r * 4;
+          float* tile = reinterpret_cast<float*>(dst) + (bh * (size_t)p.n_blocks + nb) * 16384 +
+                        (size_t)(r >> 6) * 8192 + (size_t)(r & 63) * 4;
 #pragma unroll
           for (int g = 0; g < 8; ++g)
-            red_add_v4(tile + (size_t)(c * 8 + g) * 512, __uint_as_float(a[4 * g + 0]) * mul,
+            red_add_v4(tile + (size_t)(c * 8 + g) * 256, __uint_as_float(a[4 * g + 0]) * mul,
                        __uint_as_float(a[4 * g + 1]) * mul, __uint_as_float(a[4 * g + 2]) * mul,
                        __uint_as_float(a[4 * g + 3]) * mul);
         }
@@ -411,10 +412,11 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     regs_inc<kRegsDq>();
     // ------------------------------------------------------- dQ warpgroup
     // dQ(u) leaves TMEM into registers (then the dP^T columns are free for
-    // dP(u+1)), goes through a dedicated 32 KB staging buffer in two halves
-    // and is reduced into dq_accum by one bulk cp.reduce.async per half (the
-    // accumulator's 128-row tile is [32 groups of 4 columns][128 rows][4], so
-    // a half is 32 contiguous KB).  The bulk engine, not the per-SMSP
+    // dP(u+1)), goes through a dedicated 32 KB staging buffer in two column
+    // halves and is reduced into dq_accum by two bulk cp.reduce.async per
+    // half (the accumulator's 128-row tile is [2 row halves][32 groups of 4
+    // columns][64 rows][4], so one column half of one row half is 16
+    // contiguous KB).  The bulk engine, not the per-SMSP
     // load/store pipe, carries the reduction, which keeps that pipe free for
     // the TMEM, shared-memory and mbarrier traffic of the other warps.
     const int wq = warp & 3;
@@ -445,14 +447,15 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
           for (int g = 0; g < 8; ++g)
-            *reinterpret_cast<uint4*>(xb + ((cc * 8 + g) * 128 + r) * 16) =
+            *reinterpret_cast<uint4*>(xb + (((r >> 6) * 16 + cc * 8 + g) * 64 + (r & 63)) * 16) =
                 make_uint4(q[2 * half + cc][4 * g + 0], q[2 * half + cc][4 * g + 1], q[2 * half + cc][4 * g + 2],
                            q[2 * half + cc][4 * g + 3]);
         fence_proxy_async_smem();
         mbar_arrive(bar(kBarXchgFull));
         if (leader) {
           if (!mbar_wait(bar(kBarXchgFull), (2 * u + half) & 1, abort_flag, kRoleDq, 15)) break;
-          bulk_reduce_add_f32(tile + half * 8192, sx, 32768);
+          bulk_reduce_add_f32(tile + half * 4096, sx, 16384);
+          bulk_reduce_add_f32(tile + 8192 + half * 4096, sx + 16384, 16384);
           bulk_commit_group();
         }
       }

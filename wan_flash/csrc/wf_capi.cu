@@ -80,6 +80,8 @@ int device_setup(int* dev_out) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd smem)");
   e = cudaFuncSetAttribute(wf_bwd_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd smem)");
+  e = cudaFuncSetAttribute(wf_bwd2_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd2_smem_bytes());
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd pair smem)");
   g_dev_sms[dev] = sms;
   g_dev_ready[dev] = true;
   return WF_OK;
@@ -88,14 +90,14 @@ int device_setup(int* dev_out) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // 4-D map over a contiguous (b, s, h, 128) bf16 tensor: dims {d, s, h, b},
-// box {64, 128, 1, 1} with the 128-byte swizzle (one 128-row x 128-byte box).
-int make_bshd_map(CUtensorMap* map, const void* ptr, int b, int s, int h) {
+// box {64, rows, 1, 1} with the 128-byte swizzle (rows x 128-byte box).
+int make_bshd_map(CUtensorMap* map, const void* ptr, int b, int s, int h, int rows = 128) {
   EncodeTiledFn enc;
   int rc = get_encode(&enc);
   if (rc) return rc;
   const cuuint64_t dims[4] = {128, (cuuint64_t)s, (cuuint64_t)h, (cuuint64_t)b};
   const cuuint64_t strides[3] = {(cuuint64_t)h * 256, 256, (cuuint64_t)s * h * 256};
-  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t box[4] = {64, (cuuint32_t)rows, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -257,6 +259,8 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
       !aligned16(dpsum) || !aligned16(dq_accum) || !aligned16(dk) || !aligned16(dv))
     return fail(WF_ERR_MISALIGNED, "all buffers must be 16-byte aligned");
   const int nsplit = cfg ? cfg->nsplit : 1;
+  const int cluster_n = cfg ? cfg->cluster_n : 0;
+  if (cluster_n < 0 || cluster_n > 2) return fail(WF_ERR_INVALID_ARG, "cluster_n=%d must be 0 (auto), 1 or 2", cluster_n);
   int dev;
   if ((rc = device_setup(&dev))) return rc;
   BwdParams p;
@@ -282,13 +286,36 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
       (rc = make_bshd_map(&mv, v, b, skv, h)) || (rc = make_bshd_map(&mdo, dO, b, sq, h)))
     return rc;
   const int splits = (p.m_blocks + p.m_chunk - 1) / p.m_chunk;  // every split owns >= 1 m-block
-  p.n_blocks_padded = p.n_blocks;
-  dim3 grid(p.n_blocks * splits, h, b);
-  wf_bwd_main_kernel<<<grid, kBwdThreads, bwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mdo,
-                                                                                                       p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_main launch");
-  return launch_check("wf_bwd_main launch");
+  const bool use_pair = (cluster_n == 0 ? kBwdPairDefault : cluster_n == 2);
+  if (!use_pair) {
+    p.n_blocks_padded = p.n_blocks;
+    dim3 grid(p.n_blocks * splits, h, b);
+    wf_bwd_main_kernel<<<grid, kBwdThreads, bwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv,
+                                                                                                         mdo, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_main launch");
+    return launch_check("wf_bwd_main launch");
+  }
+  // CTA pairs over adjacent KV blocks (cluster of 2, 2-SM MMAs)
+  CUtensorMap mq64, mdo64;
+  if ((rc = make_bshd_map(&mq64, q, b, sq, h, 64)) || (rc = make_bshd_map(&mdo64, dO, b, sq, h, 64))) return rc;
+  const int n_pairs = (p.n_blocks + 1) / 2;
+  p.n_blocks_padded = 2 * n_pairs;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(2 * n_pairs * splits, h, b);
+  lc.blockDim = dim3(kBwdThreads, 1, 1);
+  lc.dynamicSmemBytes = bwd2_smem_bytes();
+  lc.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&lc, wf_bwd2_main_kernel, mq, mq64, mk, mv, mdo, mdo64, p);
+  if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_main (pair) launch");
+  return launch_check("wf_bwd_main (pair) launch");
 }
 
 int wf_bwd_convert(const float* accum, void* out, float scale, int b, int s, int h, void* stream) {

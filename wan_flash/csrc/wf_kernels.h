@@ -38,6 +38,10 @@ __global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __
 __global__ void wf_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                                    BwdParams p);
+__global__ void wf_bwd2_main_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_q64,
+                                    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                                    const __grid_constant__ CUtensorMap tm_do,
+                                    const __grid_constant__ CUtensorMap tm_do64, BwdParams p);
 __global__ void wf_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
                                   const float* __restrict__ lse, float* __restrict__ dpsum,
                                   float* __restrict__ neg_lse_log2, float* __restrict__ dq_accum, int sq,
@@ -47,6 +51,10 @@ __global__ void wf_convert_kernel(const float* __restrict__ accum, __nv_bfloat16
 
 size_t fwd_smem_bytes();
 size_t bwd_smem_bytes();
+size_t bwd2_smem_bytes();
+
+// wf_bwd_main with cluster_n = 0 (auto): true = the CTA-pair kernel.
+constexpr bool kBwdPairDefault = false;
 
 constexpr int kFwdThreads = 384;
 constexpr int kBwdThreads = 512;

@@ -4,5 +4,6 @@
 #include "wf_capi.cu"
 #include "wf_fwd.cu"
 #include "wf_bwd.cu"
+#include "wf_bwd2.cu"
 #include "wf_aux.cu"
 #include "wf_noalloc.cu"

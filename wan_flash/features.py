@@ -26,7 +26,14 @@ Backward flags
                           smallest split with >= 95% wave efficiency).  With
                           nsplit > 1 dK/dV go through fp32 reductions and a
                           convert, which makes them nondeterministic.
-  cluster_n               1 only (no multicast).
+  cluster_n               1 = one CTA per 128-row KV block; 2 = CTA pairs over
+                          adjacent KV blocks of a head (cluster of 2): the
+                          pair issues 2-SM tensor-core MMAs over its 256 KV
+                          rows, each CTA loading and reading half of every
+                          Q / dO tile and the pair reducing one dQ partial
+                          per 256 KV rows.  Same purpose as the reference's
+                          cluster_n = 2 (halve the Q/dO stream), reached
+                          without multicast loads.
 """
 
 from dataclasses import dataclass, replace
@@ -79,8 +86,8 @@ def _validate_bwd(f: BwdFeatures):
         raise ValueError("the backward double-buffers Q/dO (num_stages=2)")
     if f.nsplit < 0:
         raise ValueError("nsplit must be >= 0 (0 = auto)")
-    if f.cluster_n != 1:
-        raise ValueError("cluster_n must be 1: this build issues no multicast TMA loads")
+    if f.cluster_n not in (1, 2):
+        raise ValueError("cluster_n must be 1 (single CTAs) or 2 (CTA pairs)")
 
 
 def get() -> FwdFeatures:

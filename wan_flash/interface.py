@@ -131,7 +131,7 @@ def bwd_plan(b: int, sq: int, skv: int, h: int, sms: int | None = None) -> dict:
     nsplit = max(1, min(nsplit, m_blocks))
     return {
         "sq_rounded": sq_rounded, "m_blocks": m_blocks, "n_blocks": n_blocks,
-        "skv_rounded": skv_rounded, "nsplit": nsplit,
+        "skv_rounded": skv_rounded, "nsplit": nsplit, "cluster_n": f.cluster_n,
     }
 
 
@@ -185,7 +185,7 @@ def _bwd_impl(q, k, v, o, lse, do, marks=None):
 
     L = _lib.lib()
     stream = ctypes.c_void_p(_stream_ptr(dev))
-    cfg = _lib.BwdCfg(nsplit)
+    cfg = _lib.BwdCfg(nsplit, plan["cluster_n"])
     with torch.cuda.device(dev):
         _mark(marks, "bwd_pre")
         _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(neg_lse_log2), _ptr(dq_accum),
