@@ -129,6 +129,11 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   const int m_begin = split * p.m_chunk;
   const int m_end = min(m_begin + p.m_chunk, p.m_blocks);
   const int cnt = m_end - m_begin;
+  // Query-block order, rotated per KV tile: CTAs that run at the same time
+  // then load different Q/dO tiles and reduce into different dQ tiles,
+  // instead of every resident CTA of a head hitting the same L2 lines.
+  const int rot = cnt > 0 ? nb % cnt : 0;
+  auto qblock = [&](int u) -> int { int j = u + rot; return m_begin + (j >= cnt ? j - cnt : j); };
   if (cnt <= 0) return;  // empty split: nothing to add (uniform for the CTA)
   const size_t bh = (size_t)b * p.h + h;
 
@@ -168,7 +173,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       int issued0 = 0, issued1 = 0, issued_do = 0;  // completed uses per buffer (for the abort drain)
       for (int u = 0; u < cnt; ++u) {
         const int st = u & 1, use = u >> 1;
-        const int m = m_begin + u;
+        const int m = qblock(u);
         if (use > 0 && !mbar_wait(bar(kBarQEmpty + st), (use - 1) & 1, abort_flag, kRoleBwdLoad, 3 + st)) break;
         const uint32_t qfull = bar(kBarQFull + st);
         mbar_expect_tx(qfull, kTileBytes + 1024);
@@ -195,7 +200,9 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   } else if (warp == 12) {
     regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ MMA
-    if (lane == 0) {
+    // (converged warp: every lane computes descriptors and waits, one
+    // elected lane issues each tcgen05 instruction)
+    {
       constexpr uint32_t id_kk = idesc_bf16(128, 128, 0, 0);  // A, B K-major
       constexpr uint32_t id_kb = idesc_bf16(128, 128, 0, 1);  // A K-major (or TMEM), B MN-major
       constexpr uint32_t id_mm = idesc_bf16(128, 128, 1, 1);  // A, B MN-major
@@ -213,19 +220,19 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       auto issue_s = [&](int st) {  // S^T = K Q^T
         const uint64_t q_k = sdesc(sbase + kOffQ + st * kTileBytes, 16, 1024);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) mma_ss(tS, desc_add(dK_k, koff(ks)), desc_add(q_k, koff(ks)), id_kk, ks > 0);
-        mma_commit(bar(kBarSFull));
+        for (int ks = 0; ks < 8; ++ks) mma_ss_e(tS, desc_add(dK_k, koff(ks)), desc_add(q_k, koff(ks)), id_kk, ks > 0);
+        mma_commit_e(bar(kBarSFull));
       };
       const uint64_t do_k = sdesc(sbase + kOffdO, 16, 1024);
       const uint64_t do_mn = sdesc(sbase + kOffdO, kBoxBytes, 1024);
       auto issue_dp = [&]() {  // dP^T = V dO^T
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, desc_add(dV_k, koff(ks)), desc_add(do_k, koff(ks)), id_kk, ks > 0);
-        mma_commit(bar(kBarDpFull));
+        for (int ks = 0; ks < 8; ++ks) mma_ss_e(tdP, desc_add(dV_k, koff(ks)), desc_add(do_k, koff(ks)), id_kk, ks > 0);
+        mma_commit_e(bar(kBarDpFull));
       };
-      bool ok = mbar_wait(bar(kBarKvFull), 0, abort_flag, kRoleBwdMma, 0) &&
-                mbar_wait(bar(kBarQFull + 0), 0, abort_flag, kRoleBwdMma, 1) &&
-                mbar_wait(bar(kBarDoFull), 0, abort_flag, kRoleBwdMma, 5);
+      bool ok = mbar_wait_warp(bar(kBarKvFull), 0, abort_flag, kRoleBwdMma, 0) &&
+                mbar_wait_warp(bar(kBarQFull + 0), 0, abort_flag, kRoleBwdMma, 1) &&
+                mbar_wait_warp(bar(kBarDoFull), 0, abort_flag, kRoleBwdMma, 5);
       if (ok) {
         tc_fence_after();
         issue_dp();
@@ -234,42 +241,42 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       for (int u = 0; u < cnt && ok; ++u) {
         const int st = u & 1;
         // dV += P^T dO   (P^T from TMEM: query 0-63 in columns [0,32), 64-127 in [64,96))
-        if (!(ok = mbar_wait(bar(kBarPReady), u & 1, abort_flag, kRoleBwdMma, 7))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarPReady), u & 1, abort_flag, kRoleBwdMma, 7))) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(do_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(bar(kBarDoEmpty));  // dO(u) is read by dP(u) and dV(u) only
+          mma_ts_e(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(do_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+        mma_commit_e(bar(kBarDoEmpty));  // dO(u) is read by dP(u) and dV(u) only
         // S^T(u+1): the S columns are free once dV(u) has read P^T(u)
         if (u + 1 < cnt) {
-          if (!(ok = mbar_wait(bar(kBarQFull + ((u + 1) & 1)), ((u + 1) >> 1) & 1, abort_flag, kRoleBwdMma, 1)))
+          if (!(ok = mbar_wait_warp(bar(kBarQFull + ((u + 1) & 1)), ((u + 1) >> 1) & 1, abort_flag, kRoleBwdMma, 1)))
             break;
           tc_fence_after();
           issue_s((u + 1) & 1);
         }
         // dK += dS^T Q   (dS^T from TMEM: query 0-63 in dP columns [0,32), 64-127 in [64,96))
-        if (!(ok = mbar_wait(bar(kBarDsReady), u & 1, abort_flag, kRoleBwdMma, 8))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarDsReady), u & 1, abort_flag, kRoleBwdMma, 8))) break;
         tc_fence_after();
         const uint64_t q_mn = sdesc(sbase + kOffQ + st * kTileBytes, kBoxBytes, 1024);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdK, tdP + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(q_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(bar(kBarQEmpty + st));
+          mma_ts_e(tdK, tdP + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(q_mn, moff(ks)), id_kb, (u > 0 || ks > 0) ? 1u : 0u);
+        mma_commit_e(bar(kBarQEmpty + st));
         // dQ_blk = dS K   (same dS bytes read MN-major) into the dP^T columns
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) mma_ss(tdP, desc_add(dS_mn, moff(ks)), desc_add(dK_mn, moff(ks)), id_mm, ks > 0);
-        mma_commit(bar(kBarDqFull));
-        mma_commit(bar(kBarDsEmpty));
+        for (int ks = 0; ks < 8; ++ks) mma_ss_e(tdP, desc_add(dS_mn, moff(ks)), desc_add(dK_mn, moff(ks)), id_mm, ks > 0);
+        mma_commit_e(bar(kBarDqFull));
+        mma_commit_e(bar(kBarDsEmpty));
         // dP^T(u+1) once dQ(u) has been read out of those columns and dO(u+1) is in
         if (u + 1 < cnt) {
-          if (!(ok = mbar_wait(bar(kBarDqDrained), u & 1, abort_flag, kRoleBwdMma, 11))) break;
-          if (!(ok = mbar_wait(bar(kBarDoFull), (u + 1) & 1, abort_flag, kRoleBwdMma, 5))) break;
+          if (!(ok = mbar_wait_warp(bar(kBarDqDrained), u & 1, abort_flag, kRoleBwdMma, 11))) break;
+          if (!(ok = mbar_wait_warp(bar(kBarDoFull), (u + 1) & 1, abort_flag, kRoleBwdMma, 5))) break;
           tc_fence_after();
           issue_dp();
         }
       }
-      if (ok) mma_commit(bar(kBarDkvFull));
-      mma_commit(bar(kBarDrain));
+      if (ok) mma_commit_e(bar(kBarDkvFull));
+      mma_commit_e(bar(kBarDrain));
       mbar_wait_drain(bar(kBarDrain), 0);
     }
   } else if (warp < 8) {
@@ -436,7 +443,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       for (int c = 0; c < 4; ++c) reg_fence32(q[c]);
       tc_fence_before();
       mbar_arrive(bar(kBarDqDrained));
-      float* tile = p.dq_accum + (bh * (size_t)p.m_blocks + (m_begin + u)) * 16384;
+      float* tile = p.dq_accum + (bh * (size_t)p.m_blocks + qblock(u)) * 16384;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         // the staging buffer is free once the previous bulk reduction has read it

@@ -140,6 +140,11 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
   const int m_begin = split * p.m_chunk;
   const int m_end = min(m_begin + p.m_chunk, p.m_blocks);
   const int cnt = m_end - m_begin;
+  // Query-block order, rotated per KV tile: CTAs that run at the same time
+  // then load different Q/dO tiles and reduce into different dQ tiles,
+  // instead of every resident CTA of a head hitting the same L2 lines.
+  const int rot = cnt > 0 ? pair % cnt : 0;
+  auto qblock = [&](int u) -> int { int j = u + rot; return m_begin + (j >= cnt ? j - cnt : j); };
   if (cnt <= 0) return;  // same for both CTAs of the pair
   const size_t bh = (size_t)b * p.h + h;
 
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
       int lse_issued[2] = {0, 0};
       bool ok = true;
       for (int u = 0; u < cnt && ok; ++u) {
-        const int m = m_begin + u;
+        const int m = qblock(u);
         const int qrow = m * 128;
         const int st = u & 1;
         // Q rows of this CTA for S^T(u): free once S^T(u-1) has read them
@@ -231,7 +236,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
   } else if (warp == 12) {
     regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ MMA
-    if (leader && lane == 0) {
+    if (leader) {  // converged warp: all lanes wait and form descriptors, elected lanes issue
       constexpr uint32_t id_s = idesc_bf16(256, 128, 0, 0);   // S^T, dP^T: A, B K-major
       constexpr uint32_t id_kv = idesc_bf16(256, 128, 0, 1);  // dV, dK: A in TMEM, B MN-major
       constexpr uint32_t id_q = idesc_bf16(128, 128, 1, 1);   // dQ: A, B MN-major
@@ -252,20 +257,20 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
       auto issue_s = [&]() {  // S^T = K Q^T over the pair
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss_pair(tS, desc_add(k_k, koff(ks)), desc_add(qk_k, hoff(ks)), id_s, ks > 0);
-        mma_commit_pair(bar(kBarSFull), kPairMask);
-        mma_commit_pair(bar(kBarQkEmpty), kPairMask);
+          mma_ss_pair_e(tS, desc_add(k_k, koff(ks)), desc_add(qk_k, hoff(ks)), id_s, ks > 0);
+        mma_commit_pair_e(bar(kBarSFull), kPairMask);
+        mma_commit_pair_e(bar(kBarQkEmpty), kPairMask);
       };
       auto issue_dp = [&]() {  // dP^T = V dO^T over the pair
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss_pair(tdP, desc_add(v_k, koff(ks)), desc_add(ok_k, hoff(ks)), id_s, ks > 0);
-        mma_commit_pair(bar(kBarDpFull), kPairMask);
-        mma_commit_pair(bar(kBarOkEmpty), kPairMask);
+          mma_ss_pair_e(tdP, desc_add(v_k, koff(ks)), desc_add(ok_k, hoff(ks)), id_s, ks > 0);
+        mma_commit_pair_e(bar(kBarDpFull), kPairMask);
+        mma_commit_pair_e(bar(kBarOkEmpty), kPairMask);
       };
-      bool ok = mbar_wait_cl(bar(kBarKvFull), 0, abort_flag, kRoleMma2, 0) &&
-                mbar_wait_cl(bar(kBarOkFull), 0, abort_flag, kRoleMma2, 3) &&
-                mbar_wait_cl(bar(kBarQkFull), 0, abort_flag, kRoleMma2, 1);
+      bool ok = mbar_wait_warp(bar(kBarKvFull), 0, abort_flag, kRoleMma2, 0) &&
+                mbar_wait_warp(bar(kBarOkFull), 0, abort_flag, kRoleMma2, 3) &&
+                mbar_wait_warp(bar(kBarQkFull), 0, abort_flag, kRoleMma2, 1);
       if (ok) {
         tc_fence_after();
         issue_dp();
@@ -273,45 +278,45 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
       }
       for (int u = 0; u < cnt && ok; ++u) {
         // dV += P^T dO   (P^T from TMEM: query 0-63 in columns [0,32), 64-127 in [64,96))
-        if (!(ok = mbar_wait_cl(bar(kBarPReady), u & 1, abort_flag, kRoleMma2, 5))) break;
-        if (!(ok = mbar_wait_cl(bar(kBarOnFull), u & 1, abort_flag, kRoleMma2, 4))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarPReady), u & 1, abort_flag, kRoleMma2, 5))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarOnFull), u & 1, abort_flag, kRoleMma2, 4))) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts_pair(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(on_mn, ks * 2048), id_kv,
+          mma_ts_pair_e(tdV, tS + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(on_mn, ks * 2048), id_kv,
                       (u > 0 || ks > 0) ? 1u : 0u);
-        mma_commit_pair(bar(kBarOnEmpty), kPairMask);
+        mma_commit_pair_e(bar(kBarOnEmpty), kPairMask);
         // S^T(u+1): the S columns are free once dV(u) has read P^T(u)
         if (u + 1 < cnt) {
-          if (!(ok = mbar_wait_cl(bar(kBarQkFull), (u + 1) & 1, abort_flag, kRoleMma2, 1))) break;
+          if (!(ok = mbar_wait_warp(bar(kBarQkFull), (u + 1) & 1, abort_flag, kRoleMma2, 1))) break;
           tc_fence_after();
           issue_s();
         }
         // dK += dS^T Q   (dS^T from TMEM over the dP^T columns)
-        if (!(ok = mbar_wait_cl(bar(kBarDsReady), u & 1, abort_flag, kRoleMma2, 6))) break;
-        if (!(ok = mbar_wait_cl(bar(kBarQnFull), u & 1, abort_flag, kRoleMma2, 2))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarDsReady), u & 1, abort_flag, kRoleMma2, 6))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarQnFull), u & 1, abort_flag, kRoleMma2, 2))) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts_pair(tdK, tdP + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(qn_mn, ks * 2048), id_kv,
+          mma_ts_pair_e(tdK, tdP + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(qn_mn, ks * 2048), id_kv,
                       (u > 0 || ks > 0) ? 1u : 0u);
-        mma_commit_pair(bar(kBarQnEmpty), kPairMask);
+        mma_commit_pair_e(bar(kBarQnEmpty), kPairMask);
         // dQ rows of each CTA = dS K over the pair's 256 KV rows, into the dP^T columns
 #pragma unroll
         for (int ks = 0; ks < 16; ++ks)
-          mma_ss_pair(tdP, desc_add(ds_mn, ks * 2048), desc_add(kd_mn, ks * 2048), id_q, ks > 0);
-        mma_commit_pair(bar(kBarDqFull), kPairMask);
-        mma_commit_pair(bar(kBarDsEmpty), kPairMask);
+          mma_ss_pair_e(tdP, desc_add(ds_mn, ks * 2048), desc_add(kd_mn, ks * 2048), id_q, ks > 0);
+        mma_commit_pair_e(bar(kBarDqFull), kPairMask);
+        mma_commit_pair_e(bar(kBarDsEmpty), kPairMask);
         // dP^T(u+1) once both CTAs have drained dQ(u) from those columns
         if (u + 1 < cnt) {
-          if (!(ok = mbar_wait_cl(bar(kBarDqDrained), u & 1, abort_flag, kRoleMma2, 7))) break;
-          if (!(ok = mbar_wait_cl(bar(kBarOkFull), (u + 1) & 1, abort_flag, kRoleMma2, 3))) break;
+          if (!(ok = mbar_wait_warp(bar(kBarDqDrained), u & 1, abort_flag, kRoleMma2, 7))) break;
+          if (!(ok = mbar_wait_warp(bar(kBarOkFull), (u + 1) & 1, abort_flag, kRoleMma2, 3))) break;
           tc_fence_after();
           issue_dp();
         }
       }
-      if (ok) mma_commit_pair(bar(kBarDkvFull), kPairMask);
-      mma_commit_pair(bar(kBarDrain), 0x1);
+      if (ok) mma_commit_pair_e(bar(kBarDkvFull), kPairMask);
+      mma_commit_pair_e(bar(kBarDrain), 0x1);
       mbar_wait_drain(bar(kBarDrain), 0);
     }
   } else if (warp < 8) {
@@ -329,6 +334,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
     // dS row (256 KV rows of the pair) in the smem of the CTA that owns these query columns
     const uint32_t ds_row = mapa_shared(sbase + kOffdS, (uint32_t)half);
     const uint32_t ds_r = (uint32_t)(128 * (int)rank + r);
+    const bool ds_local = (half == (int)rank);  // warp-uniform
     const uint32_t pready = lbar(kBarPReady), dsready = lbar(kBarDsReady);
     bool ok = true;
     for (int u = 0; u < cnt; ++u) {
@@ -398,12 +404,20 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
         // dS^T as the A operand of the dK MMA, over this warpgroup's dP^T columns
         tmem_st16(tdP + c * 16, pk);
         // row ds_r of dS for the dQ MMA, query columns [32c, 32c+32) of this half
+        if (ds_local) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          st_cluster_v4(ds_row + sw128_offset(ds_r, (uint32_t)(c * 4 + v)), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2],
-                        pk[4 * v + 3]);
+          for (int v = 0; v < 4; ++v)
+            *reinterpret_cast<uint4*>(smem + kOffdS + sw128_offset(ds_r, (uint32_t)(c * 4 + v))) =
+                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            st_cluster_v4(ds_row + sw128_offset(ds_r, (uint32_t)(c * 4 + v)), pk[4 * v], pk[4 * v + 1],
+                          pk[4 * v + 2], pk[4 * v + 3]);
+        }
       }
-      fence_proxy_async_cluster();
+      if (ds_local) fence_proxy_async_smem();
+      else fence_proxy_async_cluster();
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -476,7 +490,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(drained);
-      float* run = p.dq_accum + (bh * (size_t)p.m_blocks + (m_begin + u)) * 16384 + rank * 8192;
+      float* run = p.dq_accum + (bh * (size_t)p.m_blocks + qblock(u)) * 16384 + rank * 8192;
       // the staging buffer is free once the previous bulk reduction has read it
       if (lead_thr) bulk_wait_read_all();
       mbar_arrive(bar(kBarXFree));

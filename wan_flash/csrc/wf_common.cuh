@@ -101,6 +101,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Warp-uniform form for a converged warp: every lane waits and the warp
+// goes on only if all of them succeeded (the abort path stays uniform).
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                               uint32_t role, uint32_t tag) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, role, tag);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Bounded wait used only on the abort path to let in-flight copies / MMAs
 // land before the CTA releases TMEM and exits; ignores the abort flag.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
@@ -155,10 +163,14 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster
-// address (this CTA's own or a peer's).
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's own
+// or a peer's), with the instruction's default semantics.  The explicit
+// release.cluster form costs a cluster-scope memory barrier per arrival
+// (measured 1-2 us under load on B200), which the 2-SM pipelines here do not
+// need: the data they publish is ordered by tcgen05.wait::st / the proxy
+// fences that precede the arrival.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 // 16-byte store to a shared::cluster address (this CTA's or a peer's smem).
 __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -170,34 +182,6 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t a,
 __device__ __forceinline__ void fence_proxy_async_cluster() {
   asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
 }
-// try_wait with acquire at cluster scope: pairs with release.cluster arrivals
-// made by threads of a peer CTA.
-__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "n"(kSuspendHintNs)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint32_t role,
-                                             uint32_t tag) {
-  if (mbar_try_wait_cl(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  const uint64_t limit = g_wait_limit_ns;
-  while (true) {
-    if (mbar_try_wait_cl(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > limit) {
-      report_timeout(abort_flag, role, tag);
-      return false;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Named barriers (sub-CTA sync among warpgroups)
 // ---------------------------------------------------------------------------
@@ -231,6 +215,19 @@ __device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// Prefetch a tile (or a plain byte range) into L2 ahead of its load; no
+// shared memory, no completion tracking.
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -279,6 +276,21 @@ __device__ __forceinline__ void tc_fence_before() {
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// One lane of a converged warp.  The MMA-issuing warps run converged and
+// issue each tcgen05.mma / commit under elect.sync, so the descriptor
+// arithmetic around them stays warp-uniform: on B200 this halves the issue
+// time of an MMA group compared with a single diverged lane (measured ~27 vs
+// ~52 cycles per instruction).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "elect.sync _|P1, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "+r"(pred));
+  return pred != 0;
 }
 
 // D[tmem] (+)= A[smem] * B[smem]
@@ -348,6 +360,26 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask)
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
       "h"(cta_mask)
       : "memory");
+}
+
+// Elected-lane forms for a converged MMA warp (every lane must reach the call).
+__device__ __forceinline__ void mma_ss_e(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  if (elect_one()) mma_ss(d, a, b, id, acc);
+}
+__device__ __forceinline__ void mma_ts_e(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  if (elect_one()) mma_ts(d, a, b, id, acc);
+}
+__device__ __forceinline__ void mma_commit_e(uint32_t bar) {
+  if (elect_one()) mma_commit(bar);
+}
+__device__ __forceinline__ void mma_ss_pair_e(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  if (elect_one()) mma_ss_pair(d, a, b, id, acc);
+}
+__device__ __forceinline__ void mma_ts_pair_e(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  if (elect_one()) mma_ts_pair(d, a, b, id, acc);
+}
+__device__ __forceinline__ void mma_commit_pair_e(uint32_t bar, uint16_t cta_mask) {
+  if (elect_one()) mma_commit_pair(bar, cta_mask);
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -438,6 +470,10 @@ __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) {
   asm volatile("add.u64 %0, %1, %2;" : "=l"(r) : "l"(d), "l"((uint64_t)(byte_off >> 4)));
   return r;
 }
+
+// Descriptor + byte offset, visible to the compiler (warp-uniform values it
+// can keep on the uniform datapath of a converged MMA warp).
+__device__ __forceinline__ uint64_t dadd(uint64_t d, uint32_t byte_off) { return d + (uint64_t)(byte_off >> 4); }
 
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
 // a_mn / b_mn: 1 when the operand is MN-major in shared memory.

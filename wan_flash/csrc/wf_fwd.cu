@@ -185,12 +185,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   } else if (warp == 8) {
     regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ MMA
-    if (lane == 0) {
+    {  // converged warp: all lanes wait and form descriptors, elected lanes issue
       constexpr uint32_t idesc_qk = idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16(128, 128, 0, 1);
       const uint32_t sQ = sbase + kOffQ;
       const uint32_t sKV = sbase + kOffKV;
-      bool ok = mbar_wait(bar(kBarQFull), 0, abort_flag, kRoleMma, 0);
+      bool ok = mbar_wait_warp(bar(kBarQFull), 0, abort_flag, kRoleMma, 0);
       tc_fence_after();
       int pv_phase[2] = {0, 0};
       auto issue_s = [&](int t, int slot_k) {
@@ -200,13 +200,13 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t off = (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32);
-          mma_ss(d, desc_add(a0, off), desc_add(b0, off), idesc_qk, ks > 0);
+          mma_ss_e(d, desc_add(a0, off), desc_add(b0, off), idesc_qk, ks > 0);
         }
       };
       // O_t += P_t V over keys [64*half, 64*half + 64) once that half of P_t
       // has been written (P_t: bf16 pairs in S_t columns [0, 64))
       auto issue_pv_half = [&](int t, int half, int slot_v, bool acc) -> bool {
-        if (!mbar_wait(bar(kBarPFull + 2 * t + half), (uint32_t)pv_phase[t] & 1, abort_flag, kRoleMma, 20 + 2 * t + half))
+        if (!mbar_wait_warp(bar(kBarPFull + 2 * t + half), (uint32_t)pv_phase[t] & 1, abort_flag, kRoleMma, 20 + 2 * t + half))
           return false;
         tc_fence_after();
         const uint32_t d = tmem + 256u + (uint32_t)(t * 128);
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const int ks = half * 4 + kk;
-          mma_ts(d, a + ks * 8, desc_add(b0, (uint32_t)(ks * 2048)), idesc_pv, (acc || ks > 0) ? 1u : 0u);
+          mma_ts_e(d, a + ks * 8, desc_add(b0, (uint32_t)(ks * 2048)), idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
         return true;
       };
@@ -226,35 +226,35 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       };
       for (int it = 0; it < n_blocks && ok; ++it) {
         const int uk = 2 * it, slot_k = uk % kKvSlots;
-        ok = mbar_wait(bar(kBarKvFull + slot_k), (uk / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_k);
+        ok = mbar_wait_warp(bar(kBarKvFull + slot_k), (uk / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_k);
         if (!ok) break;
         tc_fence_after();
         for (int t = 0; t < 2 && ok; ++t) {
           if (it > 0) {
             const int uv = 2 * (it - 1) + 1, slot_v = uv % kKvSlots;
             if (t == 0) {
-              ok = mbar_wait(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
+              ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
               if (!ok) break;
             }
             if (!(ok = issue_pv(t, slot_v, it - 1 > 0))) break;
-            if (t == 1) mma_commit(bar(kBarKvEmpty + slot_v));
+            if (t == 1) mma_commit_e(bar(kBarKvEmpty + slot_v));
           }
           issue_s(t, slot_k);
-          mma_commit(bar(kBarSFull + t));
+          mma_commit_e(bar(kBarSFull + t));
         }
-        if (ok) mma_commit(bar(kBarKvEmpty + slot_k));
+        if (ok) mma_commit_e(bar(kBarKvEmpty + slot_k));
       }
       if (ok) {
         const int uv = 2 * (n_blocks - 1) + 1, slot_v = uv % kKvSlots;
-        ok = mbar_wait(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
+        ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
         for (int t = 0; t < 2 && ok; ++t) {
           if (!(ok = issue_pv(t, slot_v, n_blocks - 1 > 0))) break;
-          mma_commit(bar(kBarOFull + t));
+          mma_commit_e(bar(kBarOFull + t));
         }
-        if (ok) mma_commit(bar(kBarKvEmpty + slot_v));
+        if (ok) mma_commit_e(bar(kBarKvEmpty + slot_v));
       }
       // drain the tensor pipe before TMEM can be released
-      mma_commit(bar(kBarDrain));
+      mma_commit_e(bar(kBarDrain));
       mbar_wait_drain(bar(kBarDrain), 0);
     }
   } else {
