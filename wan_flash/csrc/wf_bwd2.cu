@@ -26,11 +26,21 @@
 //   warps 0-3   elementwise WG A: thread = one KV row, query columns [0, 64)
 //   warps 4-7   elementwise WG B: thread = one KV row, query columns [64, 128)
 //   warps 8-11  dQ WG: drains this CTA's 64 dQ rows (lane l holds row l%64,
-//               head-dim half l/64) and reduces them with one 32 KB bulk
-//               reduction per query block
+//               head-dim half l/64) and reduces them with two 16 KB bulk
+//               reductions per query block
 //   warp  12    TMEM owner (both CTAs); MMA issuer (leader CTA only)
-//   warp  13    TMA producer: this CTA's pieces of K, V, Q, dO; lse / D
-//   warps 14-15 idle
+//   warp  13    TMA producer A: K, V, the pair's K half; Q / dO query-row
+//               halves (S^T, dP^T operands); lse / D
+//   warp  14    dS exchange: one bulk shared::cta -> shared::cluster copy per
+//               query block of the dS rows the peer's dQ MMA needs
+//   warp  15    TMA producer B: Q / dO head-dim halves (dK, dV operands)
+//
+// dS exchange: the elementwise warpgroup whose query columns belong to the
+// peer writes its dS rows into a local 16 KB staging buffer (plain stores),
+// and warp 14 moves the block with one asynchronous bulk copy that completes
+// on the peer's mbarrier.  The leader's dQ MMA waits for its own incoming
+// block and, through a relay arrival from the peer's warp 14, for the
+// peer's; dK only waits for dS^T in TMEM.
 //
 // Synchronisation: the leader's MMA thread waits on leader-side mbarriers
 // that count both CTAs -- TMA bytes of both CTAs (cta_group::2 loads signal
@@ -58,8 +68,9 @@ constexpr uint32_t kOffQn = kOffQk + 2 * kHalfBox; // Q, 128 query rows, this CT
 constexpr uint32_t kOffOk = kOffQn + kBox;         // dO, this CTA's 64 query rows, all d        (dP^T B)
 constexpr uint32_t kOffOn = kOffOk + 2 * kHalfBox; // dO, 128 query rows, this CTA's d-half      (dV B)
 constexpr uint32_t kOffdS = kOffOn + kBox;         // dS, 256 KV rows x this CTA's 64 query cols (dQ A)
-constexpr uint32_t kOffX = kOffdS + 2 * kBox;      // dQ staging: [32 groups][64 rows][4] fp32
-constexpr uint32_t kOffLse = kOffX + 32768;        // 2 stages x 128 fp32 (-lse * log2 e)
+constexpr uint32_t kOffX = kOffdS + 2 * kBox;      // dQ staging, one head-dim half: [16 groups][64 rows][4] fp32
+constexpr uint32_t kOffDso = kOffX + 16384;        // outgoing dS rows for the peer: [128 KV rows][64 q cols] bf16
+constexpr uint32_t kOffLse = kOffDso + 16384;      // 2 stages x 128 fp32 (-lse * log2 e)
 constexpr uint32_t kOffD = kOffLse + 2 * 512;      // 2 stages x 128 fp32
 constexpr uint32_t kOffBar = kOffD + 2 * 512;
 // leader-side barriers (only the leader's copies are used)
@@ -84,10 +95,13 @@ constexpr int kBarDkvFull = 16;
 // local barriers
 constexpr int kBarLseFull = 17;   // + stage
 constexpr int kBarLseEmpty = 19;  // + stage, 8 warps
-constexpr int kBarXFull = 21;     // 128 dQ threads
-constexpr int kBarXFree = 22;     // 128 dQ threads
+constexpr int kBarXFull = 21;     // 4 dQ warps
+constexpr int kBarXFree = 22;     // 4 dQ warps
 constexpr int kBarDrain = 23;
-constexpr int kNumBars = 24;
+constexpr int kBarDsIn = 24;      // incoming dS rows from the peer (bulk-copy bytes)
+constexpr int kBarDsInPeer = 25;  // leader only: the peer's incoming block has landed (relay)
+constexpr int kBarDsoFull = 26;   // 4 warps of the warpgroup that writes the outgoing rows
+constexpr int kNumBars = 27;
 constexpr uint32_t kOffTmemHolder = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemHolder + 4;
 constexpr uint32_t kSmemUsed = kOffAbort + 4;
@@ -99,7 +113,7 @@ constexpr uint16_t kPairMask = 0x3;
 
 size_t bwd2_smem_bytes() { return bwd2::kSmemBytes; }
 
-enum : uint32_t { kRoleEw2 = 21, kRoleDq2 = 22, kRoleMma2 = 23, kRoleLoad2 = 24, kRoleEpi2 = 25 };
+enum : uint32_t { kRoleEw2 = 21, kRoleDq2 = 22, kRoleMma2 = 23, kRoleLoad2 = 24, kRoleEpi2 = 25, kRoleEx2 = 26 };
 
 __device__ __forceinline__ uint32_t dyn_smem_size2() {
   uint32_t r;
@@ -154,7 +168,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
       if (i == kBarPReady || i == kBarDsReady) count = 16;  // per-warp arrivals of both CTAs
       else if (i == kBarDqDrained) count = 8;               // 4 dQ warps of each CTA
       else if (i == kBarLseEmpty || i == kBarLseEmpty + 1) count = 8;  // this CTA's elementwise warps
-      else if (i == kBarXFull || i == kBarXFree) count = 128;
+      else if (i == kBarXFull || i == kBarXFree || i == kBarDsoFull) count = 4;  // per-warp arrivals
       mbar_init(bar(i), count);
     }
     *abort_flag = 0;
@@ -172,11 +186,49 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
   const bool leader = (rank == 0);
   auto lbar = [&](int i) -> uint32_t { return mapa_shared(bar(i), 0); };  // the leader's barrier
 
-  if (warp >= 14) {
+  if (warp == 15) {
     regs_dec<kRegsOther>();
+    // ------------------------------------------- TMA producer B (MN-major halves)
+    if (lane == 0) {
+      const int dh = 64 * (int)rank;  // this CTA's head-dim half
+      bool ok = true;
+      for (int u = 0; u < cnt && ok; ++u) {
+        const int qrow = qblock(u) * 128;
+        // dO head-dim half for dV(u): free once dV(u-1) has read it
+        if (u > 0 && !(ok = mbar_wait(bar(kBarOnEmpty), (u - 1) & 1, abort_flag, kRoleLoad2, 11))) break;
+        if (leader) mbar_expect_tx(bar(kBarOnFull), 2 * kBox);
+        tma_load_4d_pair(sbase + kOffOn, &tm_do, lbar(kBarOnFull), dh, qrow, h, b);
+        // Q head-dim half for dK(u): free once dK(u-1) has read it
+        if (u > 0 && !(ok = mbar_wait(bar(kBarQnEmpty), (u - 1) & 1, abort_flag, kRoleLoad2, 9))) break;
+        if (leader) mbar_expect_tx(bar(kBarQnFull), 2 * kBox);
+        tma_load_4d_pair(sbase + kOffQn, &tm_q, lbar(kBarQnFull), dh, qrow, h, b);
+      }
+    }
+  } else if (warp == 14) {
+    regs_dec<kRegsOther>();
+    // ------------------------------------------------------- dS exchange
+    if (lane == 0) {
+      const uint32_t peer = rank ^ 1u;
+      // this CTA's KV rows land in rows [128*rank, +128) of the peer's dS buffer
+      const uint32_t dst = mapa_shared(sbase + kOffdS + 16384u * rank, peer);
+      const uint32_t dst_bar = mapa_shared(bar(kBarDsIn), peer);
+      const uint32_t relay = lbar(kBarDsInPeer);
+      // The staging buffer needs no separate release: its writers wait for
+      // dQ(u-1) to finish (DsEmpty) before writing block u, and dQ(u-1) ran
+      // only after both CTAs' incoming blocks of u-1 had landed.  The same
+      // wait covers the peer's destination rows.
+      for (int u = 0; u < cnt; ++u) {
+        mbar_expect_tx(bar(kBarDsIn), 16384);  // arm: the peer's block for this query block
+        if (!mbar_wait(bar(kBarDsoFull), u & 1, abort_flag, kRoleEx2, 26)) break;
+        bulk_copy_to_cluster(dst, sbase + kOffDso, 16384, dst_bar);
+        // the incoming block must land before this barrier is armed again
+        if (!mbar_wait(bar(kBarDsIn), u & 1, abort_flag, kRoleEx2, 24)) break;
+        if (!leader) mbar_arrive_cluster(relay);  // the leader's dQ MMA also needs this CTA's rows
+      }
+    }
   } else if (warp == 13) {
     regs_dec<kRegsOther>();
-    // ------------------------------------------------------------------ TMA
+    // ------------------------------------------- TMA producer A (K-major halves)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_q64);
@@ -218,14 +270,6 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
         for (int x = 0; x < 2; ++x)
           tma_load_4d_pair(sbase + kOffOk + x * kHalfBox, &tm_do64, lbar(kBarOkFull), x * 64, qrow + 64 * (int)rank, h,
                            b);
-        // dO head-dim half for dV(u): free once dV(u-1) has read it
-        if (u > 0 && !(ok = mbar_wait(bar(kBarOnEmpty), (u - 1) & 1, abort_flag, kRoleLoad2, 11))) break;
-        if (leader) mbar_expect_tx(bar(kBarOnFull), 2 * kBox);
-        tma_load_4d_pair(sbase + kOffOn, &tm_do, lbar(kBarOnFull), dh, qrow, h, b);
-        // Q head-dim half for dK(u): free once dK(u-1) has read it
-        if (u > 0 && !(ok = mbar_wait(bar(kBarQnEmpty), (u - 1) & 1, abort_flag, kRoleLoad2, 9))) break;
-        if (leader) mbar_expect_tx(bar(kBarQnFull), 2 * kBox);
-        tma_load_4d_pair(sbase + kOffQn, &tm_q, lbar(kBarQnFull), dh, qrow, h, b);
       }
       if (*abort_flag) {
         // the local lse/D copies are the only ones this CTA can wait for
@@ -301,6 +345,10 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
           mma_ts_pair_e(tdK, tdP + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(qn_mn, ks * 2048), id_kv,
                       (u > 0 || ks > 0) ? 1u : 0u);
         mma_commit_pair_e(bar(kBarQnEmpty), kPairMask);
+        // dQ needs the dS rows exchanged between the CTAs: this CTA's incoming
+        // block (bulk-copy bytes) and the peer's (relayed by its warp 14)
+        if (!(ok = mbar_wait_warp(bar(kBarDsIn), u & 1, abort_flag, kRoleMma2, 24))) break;
+        if (!(ok = mbar_wait_warp(bar(kBarDsInPeer), u & 1, abort_flag, kRoleMma2, 25))) break;
         // dQ rows of each CTA = dS K over the pair's 256 KV rows, into the dP^T columns
 #pragma unroll
         for (int ks = 0; ks < 16; ++ks)
@@ -331,10 +379,10 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
     const uint32_t tdP = tmem + lane_base + 128u + (uint32_t)(half * 64);
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
-    // dS row (256 KV rows of the pair) in the smem of the CTA that owns these query columns
-    const uint32_t ds_row = mapa_shared(sbase + kOffdS, (uint32_t)half);
-    const uint32_t ds_r = (uint32_t)(128 * (int)rank + r);
+    // dS rows: query columns owned by this CTA go to row 128*rank + r of the
+    // local dS buffer; the peer's go to row r of the outgoing staging buffer
     const bool ds_local = (half == (int)rank);  // warp-uniform
+    uint8_t* const ds_base = ds_local ? smem + kOffdS + 16384 * rank : smem + kOffDso;
     const uint32_t pready = lbar(kBarPReady), dsready = lbar(kBarDsReady);
     bool ok = true;
     for (int u = 0; u < cnt; ++u) {
@@ -403,21 +451,14 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
         }
         // dS^T as the A operand of the dK MMA, over this warpgroup's dP^T columns
         tmem_st16(tdP + c * 16, pk);
-        // row ds_r of dS for the dQ MMA, query columns [32c, 32c+32) of this half
-        if (ds_local) {
+        // row r of this warpgroup's dS block, query columns [32c, 32c+32) of this half
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            *reinterpret_cast<uint4*>(smem + kOffdS + sw128_offset(ds_r, (uint32_t)(c * 4 + v))) =
-                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-        } else {
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            st_cluster_v4(ds_row + sw128_offset(ds_r, (uint32_t)(c * 4 + v)), pk[4 * v], pk[4 * v + 1],
-                          pk[4 * v + 2], pk[4 * v + 3]);
-        }
+        for (int v = 0; v < 4; ++v)
+          *reinterpret_cast<uint4*>(ds_base + sw128_offset((uint32_t)r, (uint32_t)(c * 4 + v))) =
+              make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
       }
-      if (ds_local) fence_proxy_async_smem();
-      else fence_proxy_async_cluster();
+      fence_proxy_async_smem();
+      if (!ds_local) mbar_arrive_warp(bar(kBarDsoFull));  // the exchange warp may copy the block
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -467,9 +508,10 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
     // ------------------------------------------------------- dQ warpgroup
     // This CTA's dQ rows of the pair's M = 128 MMA sit in TMEM columns
     // [128, 192): lane l holds query row 64*rank + l%64, head-dim columns
-    // [64*(l/64), +64).  They are staged as [32 groups of 4 columns][64 rows]
-    // [4] -- exactly the accumulator's 32 KB run for this row half -- and
-    // reduced by one bulk cp.reduce.async per query block.
+    // [64*(l/64), +64).  Each head-dim half is staged in turn as [16 groups
+    // of 4 columns][64 rows][4] -- one contiguous 16 KB piece of the
+    // accumulator's run for this row half -- and reduced by one bulk
+    // cp.reduce.async (two per query block).
     const int wq = warp & 3;
     const int l = wq * 32 + lane;
     const int row = l & 63, dh = l >> 6;
@@ -491,24 +533,30 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(drained);
       float* run = p.dq_accum + (bh * (size_t)p.m_blocks + qblock(u)) * 16384 + rank * 8192;
-      // the staging buffer is free once the previous bulk reduction has read it
-      if (lead_thr) bulk_wait_read_all();
-      mbar_arrive(bar(kBarXFree));
-      if (!mbar_wait(bar(kBarXFree), u & 1, abort_flag, kRoleDq2, 22)) break;
+      bool ok = true;
+      for (int hh = 0; hh < 2 && ok; ++hh) {
+        const uint32_t ph = (uint32_t)(2 * u + hh) & 1u;
+        // the staging buffer is free once the previous bulk reduction has read it
+        if (lead_thr) bulk_wait_read_all();
+        mbar_arrive_warp(bar(kBarXFree));
+        if (!(ok = mbar_wait(bar(kBarXFree), ph, abort_flag, kRoleDq2, 22))) break;
+        if (dh == hh) {  // warp-uniform: warps 0-1 hold head-dim half 0, warps 2-3 half 1
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          *reinterpret_cast<uint4*>(xb + ((dh * 16 + c * 8 + g) * 64 + row) * 16) =
-              make_uint4(q[c][4 * g + 0], q[c][4 * g + 1], q[c][4 * g + 2], q[c][4 * g + 3]);
-      fence_proxy_async_smem();
-      mbar_arrive(bar(kBarXFull));
-      if (lead_thr) {
-        if (!mbar_wait(bar(kBarXFull), u & 1, abort_flag, kRoleDq2, 21)) break;
-        bulk_reduce_add_f32(run, sx, 32768);
-        bulk_commit_group();
+            for (int g = 0; g < 8; ++g)
+              *reinterpret_cast<uint4*>(xb + ((c * 8 + g) * 64 + row) * 16) =
+                  make_uint4(q[c][4 * g + 0], q[c][4 * g + 1], q[c][4 * g + 2], q[c][4 * g + 3]);
+          fence_proxy_async_smem();
+        }
+        mbar_arrive_warp(bar(kBarXFull));
+        if (lead_thr) {
+          if (!(ok = mbar_wait(bar(kBarXFull), ph, abort_flag, kRoleDq2, 21))) break;
+          bulk_reduce_add_f32(run + hh * 4096, sx, 16384);
+          bulk_commit_group();
+        }
       }
-      if (*abort_flag) break;
+      if (!ok || *abort_flag) break;
     }
     if (lead_thr) bulk_wait_all();
   }

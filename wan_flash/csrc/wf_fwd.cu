@@ -126,8 +126,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
-      mbar_init(bar(kBarPFull + 2 * t), 128);
-      mbar_init(bar(kBarPFull + 2 * t + 1), 128);
+      mbar_init(bar(kBarPFull + 2 * t), 4);  // one arrival per softmax warp
+      mbar_init(bar(kBarPFull + 2 * t + 1), 4);
       mbar_init(bar(kBarOFull + t), 1);
     }
     mbar_init(bar(kBarDrain), 1);
@@ -328,11 +328,11 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       float bsum = fwd_exp_half(s, 0, tS, sl2x2, negx2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull + 2 * t));
+      mbar_arrive_warp(bar(kBarPFull + 2 * t));
       bsum += fwd_exp_half(s, 2, tS, sl2x2, negx2);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull + 2 * t + 1));
+      mbar_arrive_warp(bar(kBarPFull + 2 * t + 1));
       l += bsum;
     }
     // ----------------------------------------------------------- epilogue
