@@ -1,7 +1,7 @@
 """Fit the polynomial used by ``exp2_poly2`` in wf_common.cuh.
 
 Method: Cody-Waite style range reduction x = j + f with j = rint(x) and
-f in [-1/2, 1/2]; 2^x = 2^j * p(f), where p is the degree-5 polynomial that
+f in [-1/2, 1/2]; 2^x = 2^j * p(f), where p is the degree-4 polynomial that
 minimises the maximum RELATIVE error of p(f) / 2^f - 1 on [-1/2, 1/2],
 found with the Remez exchange algorithm in double precision.  The script
 prints the coefficients (rounded to fp32, as compiled into the kernels) and
@@ -46,8 +46,8 @@ def horner_f32(c32, f):
 
 
 if __name__ == "__main__":
-    c32 = remez_exp2(5).astype(np.float32)
+    c32 = remez_exp2(4).astype(np.float32)
     f = np.linspace(-0.5, 0.5, 100001).astype(np.float32)
     err = np.max(np.abs(horner_f32(c32, f).astype(np.float64) / np.exp2(f.astype(np.float64)) - 1.0))
-    print("coefficients c0..c5:", ", ".join("%.9ef" % v for v in c32))
+    print("coefficients c0..c4:", ", ".join("%.9ef" % v for v in c32))
     print("max relative error (fp32 Horner):", err)
