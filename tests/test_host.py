@@ -77,9 +77,36 @@ def test_features_defaults_overrides_and_validation():
             features.set_overrides(scheduler="lpt")
         # a rejected override leaves the state unchanged
         assert features.get().cluster_mn == (1, 1)
+        # backward kernel form: single CTAs (default) or CTA pairs
+        assert features.get_bwd().cluster_n == 1
+        features.set_bwd_overrides(cluster_n=2)
+        assert features.get_bwd().cluster_n == 2
+        with pytest.raises(ValueError):
+            features.set_bwd_overrides(cluster_n=4)
+        assert features.get_bwd().cluster_n == 2
     finally:
         features.reset()
     assert features.get() == features.FwdFeatures()
+    assert features.get_bwd() == features.BwdFeatures()
+
+
+def test_bwd_cfg_matches_c_struct_and_plan_carries_cluster_n():
+    """wf_bwd_cfg is {int nsplit; int cluster_n; int reserved[2];} in the header."""
+    import ctypes
+
+    from wan_flash import _lib, features
+    from wan_flash.interface import bwd_plan
+
+    assert ctypes.sizeof(_lib.BwdCfg) == 16
+    assert [f[0] for f in _lib.BwdCfg._fields_] == ["nsplit", "cluster_n", "reserved"]
+    cfg = _lib.BwdCfg(3, 2)
+    assert (cfg.nsplit, cfg.cluster_n, list(cfg.reserved)) == (3, 2, [0, 0])
+    try:
+        features.set_bwd_overrides(cluster_n=2)
+        assert bwd_plan(1, 32760, 32760, 12, 148)["cluster_n"] == 2
+    finally:
+        features.reset()
+    assert bwd_plan(1, 32760, 32760, 12, 148)["cluster_n"] == 1
 
 
 @pytest.mark.parametrize(
