@@ -1,6 +1,6 @@
 """Benchmark of the Wan attention hot path (forward + backward) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c3i2v|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c3i2v|c4|c5]
                     [--impl ours|reference]
 
 One step = wan_flash_fwd + wan_flash_bwd over one batch of synthetic bf16
@@ -12,7 +12,11 @@ backward (the reference's convention, bench/bench.py:89-93).
 Multi-GPU (torchrun, one rank per GPU): the work shards by heads with no
 data-path collective.  C2 runs as weak scaling (every rank owns 12 heads of a
 12*N-head problem); C4 (Wan2.1-14B 720p, 40 heads) runs as strong scaling
-(40/N heads per rank).  Time is the max over ranks of CUDA-event time.
+(40/N heads per rank).  C5 is the sequence-parallel Wan block: activations
+sequence-sharded (1, 75600/N, 40, 128) per rank, Ulysses all-to-all to head
+shards, self- and cross-attention forward + backward, all-to-all back; it
+reports the exposed communication (step time minus the same attention
+work without the exchanges).  Time is the max over ranks of CUDA-event time.
 
 Printed (rank 0): one JSON line with value (whole-job TFLOP/s, inputs
 resident in HBM), e2e (same metric through the public API with every step's
@@ -51,7 +55,12 @@ CONFIGS = {
     "c3": ("cross", 1, 75600, 512, 12, 2, "Wan2.1 cross-attention fwd+bwd (sq=75600, skv=512, h=12)"),
     "c3i2v": ("cross", 1, 75600, 257, 12, 2, "Wan2.1 I2V image cross-attention fwd+bwd (sq=75600, skv=257, h=12)"),
     "c4": ("self", 1, 75600, 75600, 40, 3, "Wan2.1-14B 720p self-attention fwd+bwd, head-sharded (b=1, s=75600, h=40)"),
+    # the sequence-parallel block: self-attention over 75600 tokens plus cross-attention against
+    # a 512-token context, activations sequence-sharded; the CPU arm samples its self-attention part
+    "c5": ("self", 1, 75600, 75600, 40, 4, "Wan2.1-14B 720p sequence-parallel block: Ulysses all-to-all, "
+           "self (75600) + cross (512) attention fwd+bwd, all-to-all back (b=1, h=40)"),
 }
+C5_CONTEXT = 512
 METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/4/8-GPU"
 # DRAM bytes (read + write) per launch per head, from one ncu capture of the
 # C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd_c2_h4.md);
@@ -188,6 +197,132 @@ def cpu_sample(cfg_name: str, target_s: float = 12.0):
     }
 
 
+# --------------------------------------------------------------------------- C5 (sequence parallel)
+def run_c5(args, rank, world, local_rank):
+    """One step = the attention of a sequence-parallel Wan block, forward and
+    backward, through wan_flash.ulysses.ulysses_attention_block: q/k/v/dO
+    sequence-sharded per rank, a 512-token context replicated, exchanges
+    overlapped with the attention work that does not need them.  Exposed
+    communication = step time minus the time of the same local attention on
+    head-sharded inputs."""
+    import torch
+    import torch.distributed as dist
+
+    from wan_flash import _lib
+    from wan_flash.interface import wan_flash_attn
+    from wan_flash.ulysses import shard_heads, ulysses_attention_block
+
+    kind, b, S, _, H, seed, desc = CONFIGS["c5"]
+    L = C5_CONTEXT
+    assert S % world == 0 and H % world == 0, "75600 tokens and 40 heads must split evenly over the ranks"
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed * 1000 + rank)
+
+    def rnd(*shape, grad=False):
+        t = torch.randn(*shape, device=dev, dtype=torch.float32, generator=gen).to(torch.bfloat16)
+        return t.requires_grad_(grad)
+
+    s_loc, hp = S // world, H // world
+    q, k, v = (rnd(b, s_loc, H, 128, grad=True) for _ in range(3))
+    do_self, do_cross = rnd(b, s_loc, H, 128), rnd(b, s_loc, H, 128)
+    gctx = torch.Generator(device=dev)
+    gctx.manual_seed(seed * 1000 + 999)  # the context is the same on every rank
+    ck, cv = (torch.randn(b, L, H, 128, device=dev, generator=gctx).to(torch.bfloat16).requires_grad_(True)
+              for _ in range(2))
+    # local (head-sharded) inputs of the same attention work, for the no-exchange reference timing
+    qh, kh, vh = (rnd(b, S, hp, 128, grad=True) for _ in range(3))
+    doh_s, doh_c = rnd(b, S, hp, 128), rnd(b, S, hp, 128)
+    ckh, cvh = (shard_heads(t.detach(), rank, world).contiguous().requires_grad_(True) for t in (ck, cv))
+
+    def sp_step():
+        for t in (q, k, v, ck, cv):
+            t.grad = None
+        if world > 1:
+            o_s, o_c = ulysses_attention_block(q, k, v, ck, cv, group)
+        else:
+            o_s, o_c = wan_flash_attn(q, k, v), wan_flash_attn(q, ck, cv)
+        torch.autograd.backward((o_s, o_c), (do_self, do_cross))
+
+    def local_step():
+        for t in (qh, kh, vh, ckh, cvh):
+            t.grad = None
+        o_s, o_c = wan_flash_attn(qh, kh, vh), wan_flash_attn(qh, ckh, cvh)
+        torch.autograd.backward((o_s, o_c), (doh_s, doh_c))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    ms = timed(sp_step)
+    clk = clocks.stop()
+    local_ms = timed(local_step)
+    _lib.check_device()
+    f_self, fb_self = flops(b, H, S, S)
+    f_cross, fb_cross = flops(b, H, S, L)
+    step_flops = f_self + fb_self + f_cross + fb_cross  # whole job (all ranks)
+    if rank == 0:
+        from wan_flash.interface import bwd_plan
+
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        launches = sum(1 + 3 + (2 if bwd_plan(b, S, skv, hp, sms)["nsplit"] > 1 else 0) for skv in (S, L))
+        peaks = load_peaks()
+        value = step_flops / (ms * 1e-3) / 1e12
+        local_tf = step_flops / world / (local_ms * 1e-3) / 1e12
+        # one all-to-all per tensor: q, k, v in; o out (x2 outputs); dO in (x2); dq, dk, dv back
+        a2a_bytes = b * s_loc * H * 128 * 2 * (world - 1) / world
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; no dataset)",
+            "config": {"workload": desc, "global_batch": b, "seq_len": S, "kv_len": S, "context_len": L,
+                       "heads_total": H, "heads_per_gpu": hp, "head_dim": 128,
+                       "parallelism": f"ulysses sp{world}",
+                       "l2": "inputs larger than L2 (activations >> 126 MB); no flush"},
+            "attention_only_ms": local_ms,
+            "attention_only_tflops_per_gpu": local_tf,
+            "exposed_comm_ms": max(0.0, ms - local_ms),
+            "exposed_comm_frac": max(0.0, ms - local_ms) / ms,
+            "all_to_all_bytes_per_tensor_per_rank": a2a_bytes,
+            "roofline": {"kernel": "attention (fwd+bwd, local)", "bound": "tensor", "achieved": local_tf,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": local_tf / peaks["bf16_tflops"],
+                         "traffic": None},
+            "cpu_baseline": None, "e2e": None, "clocks": clk,
+            "gpu_launches": launches * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -240,6 +375,9 @@ def main():
     import torch.distributed as dist
 
     from wan_flash import _lib, features, interface
+
+    if args.config == "c5":
+        return run_c5(args, rank, world, local_rank)
 
     if args.bwd_cluster_n:
         features.set_bwd_overrides(cluster_n=args.bwd_cluster_n)

@@ -25,6 +25,23 @@ def _ref_attn(q, k, v):
     return o.transpose(1, 2)
 
 
+def _ref_fwd(q, k, v):
+    """(o, lse) of the CPU reference: lse (b, h, s) natural log."""
+    scale = q.shape[-1] ** -0.5
+    s = torch.einsum("bqhd,bkhd->bhqk", q, k) * scale
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(s, dim=-1), v)
+    return o, lse
+
+
+def _ref_bwd(q, k, v, o, lse, do):
+    qq, kk, vv = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+    with torch.enable_grad():
+        oo, _ = _ref_fwd(qq, kk, vv)
+        oo.backward(do)
+    return qq.grad, kk.grad, vv.grad
+
+
 def _worker(rank, world, port, result_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -75,6 +92,21 @@ def _worker(rank, world, port, result_q):
         # every replica of the context receives the full gradient (all heads, all queries)
         torch.testing.assert_close(ckl.grad, ckf.grad, rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(cvl.grad, cvf.grad, rtol=1e-4, atol=1e-5)
+
+        # the whole block (self + cross sharing one exchanged q, overlapped exchanges)
+        qb, kb, vb = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
+        ckb, cvb = ck.clone().requires_grad_(True), cv.clone().requires_grad_(True)
+        o_s, o_c = ulysses.ulysses_attention_block(qb, kb, vb, ckb, cvb, fwd=_ref_fwd, bwd=_ref_bwd)
+        torch.autograd.backward((o_s, o_c), (go[:, sl], go2[:, sl]))
+        qf3, kf3, vf3, ckf3, cvf3 = (t.clone().requires_grad_(True) for t in (q, k, v, ck, cv))
+        os_f, oc_f = _ref_attn(qf3, kf3, vf3), _ref_attn(qf3, ckf3, cvf3)
+        torch.autograd.backward((os_f, oc_f), (go, go2))
+        torch.testing.assert_close(o_s, os_f[:, sl].detach(), rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(o_c, oc_f[:, sl].detach(), rtol=1e-5, atol=1e-5)
+        for g, gf in zip((qb.grad, kb.grad, vb.grad), (qf3.grad, kf3.grad, vf3.grad)):
+            torch.testing.assert_close(g, gf[:, sl], rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(ckb.grad, ckf3.grad, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(cvb.grad, cvf3.grad, rtol=1e-4, atol=1e-5)
         result_q.put((rank, "ok"))
     except Exception as e:  # report to the parent
         result_q.put((rank, repr(e)))

@@ -66,6 +66,18 @@ def _worker(rank, world, port, q_):
         of2.backward(go.to(dev))
         errs += [rel(o2, of2[:, sl].detach()), rel(ql2.grad, qf2.grad[:, sl]), rel(ckl.grad, ckf.grad),
                  rel(cvl.grad, cvf.grad)]
+        # the whole block: one exchanged q for both attentions, overlapped exchanges
+        go2 = torch.randn(b, S, H, D, dtype=torch.float32).to(torch.bfloat16)
+        qb, kb, vb = (t[:, sl].to(dev).requires_grad_(True) for t in (q, k, v))
+        ckb, cvb = ck.to(dev).requires_grad_(True), cv.to(dev).requires_grad_(True)
+        o_s, o_c = ulysses.ulysses_attention_block(qb, kb, vb, ckb, cvb)
+        torch.autograd.backward((o_s, o_c), (go[:, sl].to(dev), go2[:, sl].to(dev)))
+        qf3, kf3, vf3, ckf3, cvf3 = (t.to(dev).requires_grad_(True) for t in (q, k, v, ck, cv))
+        os_f, oc_f = wan_flash_attn(qf3, kf3, vf3), wan_flash_attn(qf3, ckf3, cvf3)
+        torch.autograd.backward((os_f, oc_f), (go.to(dev), go2.to(dev)))
+        errs += [rel(o_s, os_f[:, sl].detach()), rel(o_c, oc_f[:, sl].detach())]
+        errs += [rel(g, gf[:, sl]) for g, gf in zip((qb.grad, kb.grad, vb.grad), (qf3.grad, kf3.grad, vf3.grad))]
+        errs += [rel(ckb.grad, ckf3.grad), rel(cvb.grad, cvf3.grad)]
         q_.put((rank, errs))
     except Exception as e:  # report to the parent
         q_.put((rank, repr(e)))
