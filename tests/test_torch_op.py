@@ -1,0 +1,64 @@
+"""The attention as torch.library custom ops (wan_flash.torch_op).
+
+CPU: the fake implementations trace forward and backward under
+FakeTensorMode with the contract's shapes and dtypes (no kernel runs).
+GPU: the ops return exactly what wan_flash_fwd / wan_flash_bwd return, pass
+torch.library.opcheck, and the op-based autograd matches wan_flash_attn.
+"""
+
+import pytest
+import torch
+
+
+def _fake_inputs(sq=300, skv=200, h=2):
+    q = torch.empty(1, sq, h, 128, dtype=torch.bfloat16, device="cuda")
+    k = torch.empty(1, skv, h, 128, dtype=torch.bfloat16, device="cuda")
+    v = torch.empty(1, skv, h, 128, dtype=torch.bfloat16, device="cuda")
+    return q, k, v
+
+
+def test_fake_forward_backward_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import wan_flash.torch_op as op
+
+    with FakeTensorMode():
+        q, k, v = _fake_inputs()
+        o, lse = torch.ops.wan_flash.attn_fwd(q, k, v)
+        assert o.shape == q.shape and o.dtype == torch.bfloat16
+        assert lse.shape == (1, 2, 300) and lse.dtype == torch.float32
+        dq, dk, dv = torch.ops.wan_flash.attn_bwd(q, k, v, o, lse, o)
+        assert (dq.shape, dk.shape, dv.shape) == (q.shape, k.shape, v.shape)
+    # the registered autograd formula, on meta tensors (the autograd engine
+    # wants a real CUDA device for fake CUDA tensors)
+    qg, kg, vg = (torch.empty(1, s, 2, 128, dtype=torch.bfloat16, device="meta", requires_grad=True)
+                  for s in (300, 200, 200))
+    out = op.wan_attention(qg, kg, vg)
+    out.backward(torch.empty_like(out))
+    assert out.shape == qg.shape
+    assert (qg.grad.shape, kg.grad.shape, vg.grad.shape) == (qg.shape, kg.shape, vg.shape)
+    assert qg.grad.dtype == torch.bfloat16
+
+
+@pytest.mark.gpu
+def test_ops_match_interface_and_opcheck():
+    import wan_flash.torch_op as op
+    from tests.gpu_util import seeded
+    from wan_flash.interface import wan_flash_attn, wan_flash_bwd, wan_flash_fwd
+
+    q, k, v, do = (t.cuda() for t in seeded(1, 700, 300, 2, seed=23))
+    o, lse = torch.ops.wan_flash.attn_fwd(q, k, v)
+    o2, lse2 = wan_flash_fwd(q, k, v)
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)
+    g = torch.ops.wan_flash.attn_bwd(q, k, v, o, lse, do)
+    g2 = wan_flash_bwd(q, k, v, o, lse, do)
+    assert torch.equal(g[1], g2[1]) and torch.equal(g[2], g2[2])  # dq: fp32 reduction order may differ
+    assert ((g[0].float() - g2[0].float()).norm() / g2[0].float().norm()).item() < 1e-3
+    torch.library.opcheck(torch.ops.wan_flash.attn_fwd.default, (q, k, v), test_utils=("test_schema", "test_faketensor"))
+
+    qa, ka, va = (t.clone().requires_grad_(True) for t in (q, k, v))
+    qb, kb, vb = (t.clone().requires_grad_(True) for t in (q, k, v))
+    op.wan_attention(qa, ka, va).backward(do)
+    wan_flash_attn(qb, kb, vb).backward(do)
+    assert torch.equal(ka.grad, kb.grad) and torch.equal(va.grad, vb.grad)
+    assert ((qa.grad.float() - qb.grad.float()).norm() / qb.grad.float().norm()).item() < 1e-3

@@ -1,0 +1,73 @@
+"""The attention as ``torch.library`` custom ops, for callers that trace.
+
+The reference exposes a ``torch.autograd.Function`` (``interface.py:199-215``);
+its consumer, the external ``wan_attention`` op, wants a registered operator
+with a fake (meta) implementation so that graphs holding it can be traced
+with fake tensors (``torch.compile``, export, activation checkpointing
+replays) without running the kernels.  This module registers
+
+    wan_flash::attn_fwd(q, k, v) -> (o, lse)
+    wan_flash::attn_bwd(q, k, v, o, lse, do) -> (dq, dk, dv)
+
+with fake implementations that only produce the contract's shapes and
+dtypes -- o like q (bf16), lse (b, h, sq) fp32, gradients like their inputs --
+and ties them together with ``register_autograd``.  The real
+implementations are ``wan_flash_fwd`` / ``wan_flash_bwd`` (the sm_100a
+kernels); nothing here computes on the CPU.
+
+``wan_attention(q, k, v) -> o`` is the op-based counterpart of
+``wan_flash_attn``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+
+
+@torch.library.custom_op("wan_flash::attn_fwd", mutates_args=())
+def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    o, lse = wan_flash_fwd(q, k, v)
+    return o, lse
+
+
+@attn_fwd.register_fake
+def _attn_fwd_fake(q, k, v):
+    b, sq, h, d = q.shape
+    torch._check(d == 128, lambda: "specialized for head_dim=128")
+    return torch.empty_like(q), q.new_empty((b, h, sq), dtype=torch.float32)
+
+
+@torch.library.custom_op("wan_flash::attn_bwd", mutates_args=())
+def attn_bwd(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, lse: torch.Tensor, do: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    dq, dk, dv = wan_flash_bwd(q, k, v, o, lse, do)
+    return dq, dk, dv
+
+
+@attn_bwd.register_fake
+def _attn_bwd_fake(q, k, v, o, lse, do):
+    return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+
+def _setup_context(ctx, inputs, output):
+    q, k, v = inputs
+    o, lse = output
+    ctx.save_for_backward(q, k, v, o, lse)
+
+
+def _backward(ctx, do, dlse):
+    # the LSE output is not differentiated (as in the reference, which returns o only)
+    q, k, v, o, lse = ctx.saved_tensors
+    dq, dk, dv = attn_bwd(q, k, v, o, lse, do.contiguous())
+    return dq, dk, dv
+
+
+attn_fwd.register_autograd(_backward, setup_context=_setup_context)
+
+
+def wan_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """o = softmax(q k^T / sqrt(128)) v through the registered operator (differentiable)."""
+    return attn_fwd(q, k, v)[0]
