@@ -54,12 +54,17 @@ typedef struct wf_fwd_cfg {
 
 /* Backward options (mirror BwdFeatures, wan_flash/features.py:45-70). */
 typedef struct wf_bwd_cfg {
-  int nsplit;    /* split-M factor >= 1; with nsplit > 1 dk/dv arguments of
-                    wf_bwd_main are fp32 accumulators (zeroed by the caller) */
-  int cluster_n; /* 0 = auto, 1 = one CTA per KV block, 2 = CTA pairs over
-                    adjacent KV blocks (cluster of 2, 2-SM tensor-core MMAs;
-                    the reference's cluster_n = 2 without multicast loads) */
-  int reserved[2];
+  int nsplit;        /* split-M factor >= 1; with nsplit > 1 dk/dv arguments of
+                        wf_bwd_main are fp32 accumulators (zeroed by the caller) */
+  int cluster_n;     /* 0 = auto, 1 = one CTA per KV block, 2 = CTA pairs over
+                        adjacent KV blocks (cluster of 2, 2-SM tensor-core MMAs;
+                        the reference's cluster_n = 2 without multicast loads) */
+  int deterministic; /* 1 = add the fp32 dQ (and split-M dK/dV) contributions in
+                        KV-block (split) order: bitwise-reproducible gradients,
+                        slower; single-CTA kernel only; needs `sem` */
+  int reserved;
+  int* sem;          /* deterministic only: b*h*(ceil(sq/128) + ceil(skv/128))
+                        int32, zeroed by the caller before each wf_bwd_main */
 } wf_bwd_cfg;
 
 /*

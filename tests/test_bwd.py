@@ -134,6 +134,26 @@ def test_bwd_cta_pair_matches_single():
         assert rel < 1e-3, (name, rel)
 
 
+@pytest.mark.parametrize("shape,nsplit", [(WanShape("self", 1, 2, 1536, 1536), 1),
+                                          (WanShape("cross", 1, 2, 3000, 385), 3)], ids=["self", "cross-splitM"])
+def test_bwd_deterministic_bitwise(shape, nsplit):
+    """deterministic=True: dq (and split-M dk/dv) are bitwise identical run to run and within tolerance."""
+    from wan_flash import features
+    from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+
+    q, k, v, do = (t.cuda() for t in seeded(shape.b, shape.sq, shape.skv, shape.h, seed=29))
+    features.set_bwd_overrides(deterministic=True, nsplit=nsplit)
+    try:
+        o, lse = wan_flash_fwd(q, k, v)
+        runs = [wan_flash_bwd(q, k, v, o, lse, do) for _ in range(3)]
+        _run(shape, seed=29)
+    finally:
+        features.reset()
+    for g in runs[1:]:
+        for a, b in zip(runs[0], g):
+            assert torch.equal(a, b)
+
+
 def test_bwd_oracle_o_lse_contract():
     """Our backward consuming the oracle's o/lse (the natural-log LSE drop-in)."""
     from oracle.oracle import oracle_fwd

@@ -97,10 +97,18 @@ def test_bwd_cfg_matches_c_struct_and_plan_carries_cluster_n():
     from wan_flash import _lib, features
     from wan_flash.interface import bwd_plan
 
-    assert ctypes.sizeof(_lib.BwdCfg) == 16
-    assert [f[0] for f in _lib.BwdCfg._fields_] == ["nsplit", "cluster_n", "reserved"]
+    assert ctypes.sizeof(_lib.BwdCfg) == 24
+    assert [f[0] for f in _lib.BwdCfg._fields_] == ["nsplit", "cluster_n", "deterministic", "reserved", "sem"]
     cfg = _lib.BwdCfg(3, 2)
-    assert (cfg.nsplit, cfg.cluster_n, list(cfg.reserved)) == (3, 2, [0, 0])
+    assert (cfg.nsplit, cfg.cluster_n, cfg.deterministic, cfg.sem) == (3, 2, 0, None)
+    try:
+        features.set_bwd_overrides(deterministic=True)
+        plan = bwd_plan(1, 1000, 300, 2, 148)
+        assert plan["deterministic"] and plan["sem_len"] == 2 * (8 + 3)
+        with pytest.raises(ValueError):
+            features.set_bwd_overrides(cluster_n=2)  # pairs have no ordered mode
+    finally:
+        features.reset()
     try:
         features.set_bwd_overrides(cluster_n=2)
         assert bwd_plan(1, 32760, 32760, 12, 148)["cluster_n"] == 2

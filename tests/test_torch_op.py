@@ -52,13 +52,14 @@ def test_ops_match_interface_and_opcheck():
     assert torch.equal(o, o2) and torch.equal(lse, lse2)
     g = torch.ops.wan_flash.attn_bwd(q, k, v, o, lse, do)
     g2 = wan_flash_bwd(q, k, v, o, lse, do)
-    assert torch.equal(g[1], g2[1]) and torch.equal(g[2], g2[2])  # dq: fp32 reduction order may differ
-    assert ((g[0].float() - g2[0].float()).norm() / g2[0].float().norm()).item() < 1e-3
+    # same kernels; only the fp32 reduction order (dq, and dk/dv under split-M) may differ
+    for a, b in zip(g, g2):
+        assert ((a.float() - b.float()).norm() / b.float().norm()).item() < 1e-3
     torch.library.opcheck(torch.ops.wan_flash.attn_fwd.default, (q, k, v), test_utils=("test_schema", "test_faketensor"))
 
     qa, ka, va = (t.clone().requires_grad_(True) for t in (q, k, v))
     qb, kb, vb = (t.clone().requires_grad_(True) for t in (q, k, v))
     op.wan_attention(qa, ka, va).backward(do)
     wan_flash_attn(qb, kb, vb).backward(do)
-    assert torch.equal(ka.grad, kb.grad) and torch.equal(va.grad, vb.grad)
-    assert ((qa.grad.float() - qb.grad.float()).norm() / qb.grad.float().norm()).item() < 1e-3
+    for a, b in zip((qa.grad, ka.grad, va.grad), (qb.grad, kb.grad, vb.grad)):
+        assert ((a.float() - b.float()).norm() / b.float().norm()).item() < 1e-3

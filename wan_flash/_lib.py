@@ -38,7 +38,8 @@ class FwdCfg(ctypes.Structure):
 
 
 class BwdCfg(ctypes.Structure):
-    _fields_ = [("nsplit", ctypes.c_int), ("cluster_n", ctypes.c_int), ("reserved", ctypes.c_int * 2)]
+    _fields_ = [("nsplit", ctypes.c_int), ("cluster_n", ctypes.c_int), ("deterministic", ctypes.c_int),
+                ("reserved", ctypes.c_int), ("sem", ctypes.c_void_p)]
 
 
 class WanFlashError(RuntimeError):

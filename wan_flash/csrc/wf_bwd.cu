@@ -76,7 +76,9 @@ constexpr int kBarDkvFull = 14;
 constexpr int kBarDrain = 15;
 constexpr int kBarXchgFull = 16;   // the dQ warpgroup has written a half-tile into the staging buffer
 constexpr int kBarXchgDone = 17;   // the staging buffer is free again (previous bulk read done)
-constexpr int kNumBars = 18;
+constexpr int kBarEpiGo = 18;      // deterministic split-M: earlier splits have added their dK/dV
+constexpr int kBarEpiDone = 19;    // deterministic split-M: this CTA's dK/dV reductions are issued
+constexpr int kNumBars = 20;
 constexpr uint32_t kOffTmemHolder = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemHolder + 4;
 constexpr uint32_t kSmemUsed = kOffAbort + 4;
@@ -132,7 +134,9 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   // Query-block order, rotated per KV tile: CTAs that run at the same time
   // then load different Q/dO tiles and reduce into different dQ tiles,
   // instead of every resident CTA of a head hitting the same L2 lines.
-  const int rot = cnt > 0 ? nb % cnt : 0;
+  // (deterministic mode keeps the natural order: KV block nb then meets each
+  // query block right after KV block nb-1, which it must wait for)
+  const int rot = (cnt > 0 && !p.deterministic) ? nb % cnt : 0;
   auto qblock = [&](int u) -> int { int j = u + rot; return m_begin + (j >= cnt ? j - cnt : j); };
   if (cnt <= 0) return;  // empty split: nothing to add (uniform for the CTA)
   const size_t bh = (size_t)b * p.h + h;
@@ -141,7 +145,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     for (int i = 0; i < kNumBars; ++i) {
       // per-thread arrivals (measured faster here than one arrival per warp)
       const bool ew = (i == kBarPReady || i == kBarDsReady);
-      const uint32_t count = ew ? 256u : (i == kBarDqDrained || i == kBarXchgDone || i == kBarXchgFull) ? 128u : 1u;
+      const uint32_t count = (ew || i == kBarEpiDone) ? 256u
+                             : (i == kBarDqDrained || i == kBarXchgDone || i == kBarXchgFull) ? 128u : 1u;
       mbar_init(bar(i), count);
     }
     *abort_flag = 0;
@@ -382,6 +387,15 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     // ----------------------------------------------------------- epilogue
     // WG A writes dV (unscaled), WG B writes dK (scaled by softmax_scale)
     if (ok) ok = mbar_wait(bar(kBarDkvFull), 0, abort_flag, kRoleEpi, 12);
+    const bool ordered = p.accum_dkv && p.deterministic;
+    int* kv_sem = ordered ? p.dkv_sem + bh * (size_t)p.n_blocks + nb : nullptr;
+    if (ok && ordered) {
+      // splits 0..split-1 add their dK/dV for this KV block first
+      if (threadIdx.x == 0) {
+        if (counter_wait_eq(kv_sem, split, abort_flag, kRoleEpi, 20)) mbar_arrive(bar(kBarEpiGo));
+      }
+      ok = mbar_wait(bar(kBarEpiGo), 0, abort_flag, kRoleEpi, 18);
+    }
     if (ok) {
       tc_fence_after();
       const int kv = n0 + r;
@@ -415,6 +429,14 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
                        __uint_as_float(a[4 * g + 3]) * mul);
         }
       }
+      if (ordered) {
+        __threadfence();
+        mbar_arrive(bar(kBarEpiDone));
+        if (threadIdx.x == 0 && mbar_wait(bar(kBarEpiDone), 0, abort_flag, kRoleEpi, 19)) {
+          __threadfence();
+          st_release_gpu(kv_sem, split + 1);
+        }
+      }
     }
   } else {
     regs_inc<kRegsDq>();
@@ -433,6 +455,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     const uint32_t sx = sbase + kOffX;
     uint8_t* xb = smem + kOffX;
     const bool leader = (threadIdx.x == 256);
+    int* const q_sem = p.deterministic ? p.dq_sem + bh * (size_t)p.m_blocks : nullptr;
     for (int u = 0; u < cnt; ++u) {
       if (!mbar_wait(bar(kBarDqFull), u & 1, abort_flag, kRoleDq, 10)) break;
       tc_fence_after();
@@ -462,9 +485,19 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         mbar_arrive(bar(kBarXchgFull));
         if (leader) {
           if (!mbar_wait(bar(kBarXchgFull), (2 * u + half) & 1, abort_flag, kRoleDq, 15)) break;
+          if (q_sem != nullptr && half == 0) {
+            // KV blocks 0..nb-1 add their contributions to this query block first
+            if (!counter_wait_eq(q_sem + qblock(u), nb, abort_flag, kRoleDq, 20)) break;
+            fence_proxy_async_global();
+          }
           bulk_reduce_add_f32(tile + half * 4096, sx, 16384);
           bulk_reduce_add_f32(tile + 8192 + half * 4096, sx + 16384, 16384);
           bulk_commit_group();
+          if (q_sem != nullptr && half == 1) {
+            bulk_wait_all();  // the reductions have landed in global memory
+            fence_proxy_async_global();
+            st_release_gpu(q_sem + qblock(u), nb + 1);
+          }
         }
       }
       if (*abort_flag) break;

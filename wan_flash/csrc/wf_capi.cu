@@ -261,6 +261,11 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
   const int nsplit = cfg ? cfg->nsplit : 1;
   const int cluster_n = cfg ? cfg->cluster_n : 0;
   if (cluster_n < 0 || cluster_n > 2) return fail(WF_ERR_INVALID_ARG, "cluster_n=%d must be 0 (auto), 1 or 2", cluster_n);
+  const int deterministic = cfg ? cfg->deterministic : 0;
+  if (deterministic && (!cfg->sem || (reinterpret_cast<uintptr_t>(cfg->sem) & 3)))
+    return fail(WF_ERR_INVALID_ARG, "deterministic mode needs a 4-byte aligned sem workspace");
+  if (deterministic && cluster_n == 2)
+    return fail(WF_ERR_UNSUPPORTED, "deterministic mode runs on the single-CTA kernel (cluster_n 0 or 1)");
   int dev;
   if ((rc = device_setup(&dev))) return rc;
   BwdParams p;
@@ -281,12 +286,15 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
   p.accum_dkv = nsplit > 1 ? 1 : 0;
   p.scale = (float)(1.0 / std::sqrt(128.0));
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  p.deterministic = deterministic ? 1 : 0;
+  p.dq_sem = deterministic ? cfg->sem : nullptr;
+  p.dkv_sem = deterministic ? cfg->sem + (size_t)b * h * p.m_blocks : nullptr;
   CUtensorMap mq, mk, mv, mdo;
   if ((rc = make_bshd_map(&mq, q, b, sq, h)) || (rc = make_bshd_map(&mk, k, b, skv, h)) ||
       (rc = make_bshd_map(&mv, v, b, skv, h)) || (rc = make_bshd_map(&mdo, dO, b, sq, h)))
     return rc;
   const int splits = (p.m_blocks + p.m_chunk - 1) / p.m_chunk;  // every split owns >= 1 m-block
-  const bool use_pair = (cluster_n == 0 ? kBwdPairDefault : cluster_n == 2);
+  const bool use_pair = !deterministic && (cluster_n == 0 ? kBwdPairDefault : cluster_n == 2);
   if (!use_pair) {
     p.n_blocks_padded = p.n_blocks;
     dim3 grid(p.n_blocks * splits, h, b);

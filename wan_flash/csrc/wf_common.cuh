@@ -116,6 +116,36 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
   return __all_sync(0xffffffffu, ok);
 }
 
+// Global-memory counters for ordered accumulation (deterministic mode).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Order generic-proxy and async-proxy (bulk copy / reduction) accesses to global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bounded wait until *p == want (one polling thread, backing off with nanosleep).
+__device__ __forceinline__ bool counter_wait_eq(const int* p, int want, volatile int* abort_flag, uint32_t role,
+                                                uint32_t tag) {
+  if (ld_acquire_gpu(p) == want) return true;
+  const uint64_t t0 = globaltimer();
+  const uint64_t limit = g_wait_limit_ns;
+  while (true) {
+    __nanosleep(200);
+    if (ld_acquire_gpu(p) == want) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > limit) {
+      report_timeout(abort_flag, role, tag);
+      return false;
+    }
+  }
+}
+
 // Bounded wait used only on the abort path to let in-flight copies / MMAs
 // land before the CTA releases TMEM and exits; ignores the abort flag.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {

@@ -31,6 +31,9 @@ struct BwdParams {
   int m_chunk;             // split-M: m-blocks per CTA
   float scale;             // 1/sqrt(128)
   float scale_log2;        // log2(e)/sqrt(128)
+  int* dq_sem;             // deterministic: (b*h, m_blocks) dQ contributions added so far
+  int* dkv_sem;            // deterministic, split-M: (b*h, n_blocks) splits added so far
+  int deterministic;
 };
 
 __global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,

@@ -83,7 +83,7 @@ extern "C" int wf_bwd_noalloc(const void* q, const void* k, const void* v, const
   float* neg_lse_log2 = dpsum + rows;
   float* dq_accum = neg_lse_log2 + rows;
   if ((rc = wf_bwd_pre(o, dO, lse, dpsum, neg_lse_log2, dq_accum, b, sq, (int)sq_rounded, h, stream))) return rc;
-  wf_bwd_cfg cfg = {1, 0, {0, 0}};
+  wf_bwd_cfg cfg = {1, 0, 0, 0, nullptr};
   if ((rc = wf_bwd_main(q, k, v, dO, neg_lse_log2, dpsum, dq_accum, dk, dv, b, sq, skv, h, &cfg, stream))) return rc;
   return wf_bwd_convert(dq_accum, dq, (float)(1.0 / std::sqrt(128.0)), b, sq, h, stream);
 }

@@ -34,6 +34,11 @@ Backward flags
                           per 256 KV rows.  Same purpose as the reference's
                           cluster_n = 2 (halve the Q/dO stream), reached
                           without multicast loads.
+  deterministic           False (default): dQ (and split-M dK/dV) are fp32
+                          reductions in arrival order.  True: contributions
+                          are added in KV-block (split) order behind
+                          per-block counters, so every gradient is bitwise
+                          reproducible; slower, single-CTA kernel only.
 """
 
 from dataclasses import dataclass, replace
@@ -58,6 +63,7 @@ class BwdFeatures:
     num_stages: int = 2
     nsplit: int = 0
     cluster_n: int = 1
+    deterministic: bool = False
 
 
 _current = FwdFeatures()
@@ -88,6 +94,8 @@ def _validate_bwd(f: BwdFeatures):
         raise ValueError("nsplit must be >= 0 (0 = auto)")
     if f.cluster_n not in (1, 2):
         raise ValueError("cluster_n must be 1 (single CTAs) or 2 (CTA pairs)")
+    if f.deterministic and f.cluster_n != 1:
+        raise ValueError("deterministic mode runs on the single-CTA kernel (cluster_n=1)")
 
 
 def get() -> FwdFeatures:

@@ -132,6 +132,9 @@ def bwd_plan(b: int, sq: int, skv: int, h: int, sms: int | None = None) -> dict:
     return {
         "sq_rounded": sq_rounded, "m_blocks": m_blocks, "n_blocks": n_blocks,
         "skv_rounded": skv_rounded, "nsplit": nsplit, "cluster_n": f.cluster_n,
+        "deterministic": bool(f.deterministic),
+        # deterministic mode: ordered-accumulation counters, (b*h) x (m_blocks + n_blocks) int32
+        "sem_len": b * h * (m_blocks + n_blocks) if f.deterministic else 0,
     }
 
 
@@ -186,6 +189,9 @@ def _bwd_impl(q, k, v, o, lse, do, marks=None):
     L = _lib.lib()
     stream = ctypes.c_void_p(_stream_ptr(dev))
     cfg = _lib.BwdCfg(nsplit, plan["cluster_n"])
+    if plan["deterministic"]:
+        sem = torch.zeros(plan["sem_len"], device=dev, dtype=torch.int32)
+        cfg.deterministic, cfg.sem = 1, sem.data_ptr()
     with torch.cuda.device(dev):
         _mark(marks, "bwd_pre")
         _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(neg_lse_log2), _ptr(dq_accum),
