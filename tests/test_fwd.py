@@ -115,6 +115,43 @@ def test_fwd_noncontiguous_and_stream():
     assert torch.equal(o, o_ref) and torch.equal(lse, lse_ref)
 
 
+SCHED_SHAPES = [(2048, 512, 2), (2048, 257, 2), (1152, 1152, 2), (385, 1, 3), (700, 130, 3)]
+
+
+@pytest.mark.parametrize("sq,skv,h", SCHED_SHAPES, ids=lambda x: str(x))
+@pytest.mark.parametrize("num_sms", [0, 1, 5])
+def test_fwd_persistent_matches_single(sq, skv, h, num_sms):
+    """The persistent grid (a CTA loops over work items with its barrier
+    phases, K/V ring and TMEM carried across items) gives bitwise the output
+    of one CTA per item; num_sms=1 puts every item on one CTA."""
+    from wan_flash import _lib, features
+    from wan_flash.interface import wan_flash_fwd
+
+    q, k, v, _ = seeded(2, sq, skv, h, seed=sq + skv)
+    qc, kc, vc = (t.cuda() for t in (q, k, v))
+    try:
+        features.set_overrides(scheduler="single")
+        o1, l1 = wan_flash_fwd(qc, kc, vc)
+        features.set_overrides(scheduler="persistent", num_sms=num_sms)
+        o2, l2 = wan_flash_fwd(qc, kc, vc)
+        _lib.check_device()
+    finally:
+        features.reset()
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+@pytest.mark.parametrize("skv", [512, 257, 1000])
+def test_fwd_persistent_vs_oracle(skv):
+    """Persistent grid with several items per CTA against the oracle."""
+    from wan_flash import features
+
+    features.set_overrides(scheduler="persistent", num_sms=3)
+    try:
+        _run(WanShape("cross", 1, 3, 1500, skv), seed=skv)
+    finally:
+        features.reset()
+
+
 def test_fwd_deterministic():
     from wan_flash.interface import wan_flash_fwd
 

@@ -75,6 +75,11 @@ def test_features_defaults_overrides_and_validation():
             features.set_bwd_overrides(tile_m=80)
         with pytest.raises(ValueError):
             features.set_overrides(scheduler="lpt")
+        features.set_overrides(scheduler="persistent", num_sms=7)
+        assert features.get().scheduler == "persistent" and features.get().num_sms == 7
+        with pytest.raises(ValueError):
+            features.set_overrides(num_sms=-1)
+        features.set_overrides(scheduler="auto", num_sms=0)
         # a rejected override leaves the state unchanged
         assert features.get().cluster_mn == (1, 1)
         # backward kernel form: single CTAs (default) or CTA pairs

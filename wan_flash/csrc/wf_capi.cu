@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -210,9 +211,9 @@ int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
     return fail(WF_ERR_MISALIGNED, "q/k/v/o must be 16-byte aligned and lse 4-byte aligned");
   int dev;
   if ((rc = device_setup(&dev))) return rc;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if ((rc = make_bshd_map(&mq, q, b, sq, h)) || (rc = make_bshd_map(&mk, k, b, skv, h)) ||
-      (rc = make_bshd_map(&mv, v, b, skv, h)))
+      (rc = make_bshd_map(&mv, v, b, skv, h)) || (rc = make_bshd_map(&mo, o, b, sq, h)))
     return rc;
   FwdParams p;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
@@ -223,8 +224,17 @@ int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
   p.n_blocks = (skv + 127) / 128;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
   p.rescale_threshold = cfg ? cfg->rescale_threshold : 8.0f;
-  dim3 grid((sq + 255) / 256, h, b);
-  wf_fwd_kernel<<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, p);
+  p.n_pairs = (sq + 255) / 256;
+  const long long n_items = (long long)p.n_pairs * h * b;
+  if (n_items > 0x7fffffffLL) return fail(WF_ERR_UNSUPPORTED, "%lld work items exceed the grid limit", n_items);
+  p.n_items = (int)n_items;
+  const int sched = cfg ? cfg->scheduler : 0;
+  if (sched < 0 || sched > 2) return fail(WF_ERR_INVALID_ARG, "scheduler %d not in {0, 1, 2}", sched);
+  if (cfg && cfg->num_sms < 0) return fail(WF_ERR_INVALID_ARG, "num_sms %d < 0", cfg->num_sms);
+  const int sms = (cfg && cfg->num_sms > 0) ? cfg->num_sms : g_dev_sms[dev];
+  const bool persistent = sched == 2 || (sched == 0 && p.n_blocks <= kFwdPersistMaxBlocks);
+  const int grid = persistent ? (int)std::min<long long>(n_items, sms) : p.n_items;
+  wf_fwd_kernel<<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
   return launch_check("wf_fwd launch");
 }
 

@@ -9,12 +9,18 @@
 // LSE = (m * scale_log2 + log2(sum)) * ln2 (:866-876).  The schedule is a
 // Blackwell design of its own:
 //
-//   CTA = 2 query tiles of 128 rows (256 rows) of one (batch, head).
+//   work item = 2 query tiles of 128 rows (256 rows) of one (batch, head).
+//   A CTA runs items blockIdx.x, blockIdx.x + gridDim.x, ...: one item per
+//   CTA (grid = all items), or persistent (grid = SM count) for short KV
+//   sequences, where the per-item prologue and epilogue would otherwise
+//   leave the tensor pipe idle: the next item's Q load overlaps the current
+//   item's last blocks and its first QK^T the current item's last PV.
 //   warps 0-3  softmax for query tile 0  (thread = one query row)
 //   warps 4-7  softmax for query tile 1
 //   warp  8    tcgen05.mma issuer (one thread) + TMEM owner
 //   warp  9    TMA producer (one thread)
-//   warps 10-11 idle (complete warpgroup 2 so it can give registers back)
+//   warp  10   O store: one thread sends each staged O tile out with TMA
+//   warp  11   idle (completes warpgroup 2 so it can give registers back)
 //
 //   TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
 //   P_t (bf16, 64 columns) overwrites the first half of S_t once S_t is read.
@@ -42,16 +48,20 @@ constexpr uint32_t kBoxBytes = 128 * 128;        // 128 rows x 64 bf16 (one 128B
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;   // 128 rows x 128 bf16
 constexpr uint32_t kOffQ = 0;                    // 2 query tiles
 constexpr uint32_t kOffKV = 2 * kTileBytes;      // kKvSlots tiles (K and V alternate)
-constexpr uint32_t kOffBar = kOffKV + kKvSlots * kTileBytes;
+constexpr uint32_t kOffOStage = kOffKV + kKvSlots * kTileBytes;  // one O tile (bf16, two swizzled boxes)
+constexpr uint32_t kOffBar = kOffOStage + kTileBytes;
 // barrier indices
-constexpr int kBarQFull = 0;
-constexpr int kBarKvFull = 1;                    // + slot
+constexpr int kBarQFull = 0;                     // + tile
+constexpr int kBarQEmpty = 2;                    // + tile
+constexpr int kBarKvFull = 4;                    // + slot
 constexpr int kBarKvEmpty = kBarKvFull + kKvSlots;
 constexpr int kBarSFull = kBarKvEmpty + kKvSlots;  // + tile
 constexpr int kBarPFull = kBarSFull + 2;      // + 2 * tile + half (keys 0-63 / 64-127)
 constexpr int kBarOFull = kBarPFull + 4;
 constexpr int kBarDrain = kBarOFull + 2;
-constexpr int kNumBars = kBarDrain + 1;
+constexpr int kBarOStaged = kBarDrain + 1;       // O tile written to the stage (one arrival per warp)
+constexpr int kBarOStageFree = kBarOStaged + 1;  // stage read by the tensor store
+constexpr int kNumBars = kBarOStageFree + 1;
 constexpr uint32_t kOffTmemHolder = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemHolder + 4;
 constexpr uint32_t kSmemUsed = kOffAbort + 4;
@@ -61,7 +71,7 @@ constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + alignment slack
 size_t fwd_smem_bytes() { return fwd::kSmemBytes; }
 
 // role ids recorded on a wait timeout
-enum : uint32_t { kRoleSoftmax0 = 1, kRoleSoftmax1 = 2, kRoleMma = 3, kRoleLoad = 4 };
+enum : uint32_t { kRoleSoftmax0 = 1, kRoleSoftmax1 = 2, kRoleMma = 3, kRoleLoad = 4, kRoleStore = 5 };
 
 // Exponentials of half a 128-column block (two 32-column chunks starting at
 // chunk c0) for this thread's row: P = 2^(s * scale_log2 - m) is stored to
@@ -101,7 +111,8 @@ __device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0
 
 __global__ void __launch_bounds__(fwd::kThreads, 1)
     wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, FwdParams p) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  FwdParams p) {
   using namespace fwd;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,13 +124,22 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 
   const int warp = (int)warp_id();
   const int lane = (int)lane_id();
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int m0 = blockIdx.x * 256;
   const int n_blocks = p.n_blocks;
+  // work item = 256 query rows (two 128-row tiles) of one (batch, head);
+  // item i covers rows 256 * (i % n_pairs) of head (i / n_pairs) % h
+  auto item_coords = [&](int item, int& m0, int& h, int& b) {
+    const int pair = item % p.n_pairs;
+    const int hb = item / p.n_pairs;
+    m0 = pair * 256;
+    h = hb % p.h;
+    b = hb / p.h;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(kBarQFull), 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kBarQFull + t), 1);
+      mbar_init(bar(kBarQEmpty + t), 1);
+    }
     for (int s = 0; s < kKvSlots; ++s) {
       mbar_init(bar(kBarKvFull + s), 1);
       mbar_init(bar(kBarKvEmpty + s), 1);
@@ -131,6 +151,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       mbar_init(bar(kBarOFull + t), 1);
     }
     mbar_init(bar(kBarDrain), 1);
+    mbar_init(bar(kBarOStaged), 4);
+    mbar_init(bar(kBarOStageFree), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -143,8 +165,33 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp >= 10) {
-    regs_dec<kRegsOther>();  // idle warps of warpgroup 2
+  if (warp == 11) {
+    regs_dec<kRegsOther>();  // idle warp of warpgroup 2
+  } else if (warp == 10) {
+    regs_dec<kRegsOther>();
+    // ------------------------------------------------------------ O store
+    // The softmax warps of tile 0 and tile 1 take turns on the one stage
+    // buffer (item order, tile 0 first: the MMA completes O_0 of an item
+    // before O_1, and O_1 before the next item's O_0).
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_o);
+      int n = 0;  // tiles stored
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+        int m0, h, b;
+        item_coords(item, m0, h, b);
+        for (int t = 0; t < 2; ++t, ++n) {
+          ok = mbar_wait(bar(kBarOStaged), (uint32_t)n & 1, abort_flag, kRoleStore, 50 + t);
+          if (!ok) break;
+          for (int x = 0; x < 2; ++x)
+            tma_store_4d(&tm_o, sbase + kOffOStage + x * kBoxBytes, x * 64, m0 + t * 128, h, b);
+          bulk_commit_group();
+          bulk_wait_read_all();
+          mbar_arrive(bar(kBarOStageFree));
+        }
+      }
+      bulk_wait_all();
+    }
   } else if (warp == 9) {
     regs_dec<kRegsOther>();
     // ------------------------------------------------------------------ TMA
@@ -152,32 +199,48 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_expect_tx(bar(kBarQFull), 2 * kTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int x = 0; x < 2; ++x)
-          tma_load_4d(sbase + kOffQ + t * kTileBytes + x * kBoxBytes, &tm_q, bar(kBarQFull), x * 64,
-                      m0 + t * 128, h, b);
-      int issued[kKvSlots] = {0, 0, 0, 0};
+      int q_issued[2] = {0, 0};                // Q loads per tile buffer
+      int issued[kKvSlots] = {0, 0, 0, 0};     // K/V loads per ring slot
+      int u = 0;                               // K/V units (K and V of a block alternate)
       bool ok = true;
-      for (int it = 0; it < n_blocks && ok; ++it) {
-        const int j = (it == 0) ? (n_blocks - 1) : (it - 1);
-        for (int kv = 0; kv < 2 && ok; ++kv) {  // 0 = K, 1 = V
-          const int u = 2 * it + kv;
-          const int slot = u % kKvSlots;
-          const int use = u / kKvSlots;
-          if (use > 0) ok = mbar_wait(bar(kBarKvEmpty + slot), (use - 1) & 1, abort_flag, kRoleLoad, 100 + slot);
-          if (!ok) break;
-          mbar_expect_tx(bar(kBarKvFull + slot), kTileBytes);
-          const CUtensorMap* tm = kv ? &tm_v : &tm_k;
-          for (int x = 0; x < 2; ++x)
-            tma_load_4d(sbase + kOffKV + slot * kTileBytes + x * kBoxBytes, tm, bar(kBarKvFull + slot),
-                        x * 64, j * 128, h, b);
-          issued[slot] = use + 1;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+        int m0, h, b;
+        item_coords(item, m0, h, b);
+        for (int it = 0; it < n_blocks && ok; ++it) {
+          const int j = (it == 0) ? (n_blocks - 1) : (it - 1);
+          for (int kv = 0; kv < 2 && ok; ++kv, ++u) {  // 0 = K, 1 = V
+            const int slot = u % kKvSlots;
+            const int use = u / kKvSlots;
+            if (use > 0) ok = mbar_wait(bar(kBarKvEmpty + slot), (use - 1) & 1, abort_flag, kRoleLoad, 100 + slot);
+            if (!ok) break;
+            mbar_expect_tx(bar(kBarKvFull + slot), kTileBytes);
+            const CUtensorMap* tm = kv ? &tm_v : &tm_k;
+            for (int x = 0; x < 2; ++x)
+              tma_load_4d(sbase + kOffKV + slot * kTileBytes + x * kBoxBytes, tm, bar(kBarKvFull + slot),
+                          x * 64, j * 128, h, b);
+            issued[slot] = use + 1;
+            if (it == 0 && kv == 0) {
+              // the item's Q tiles go between its first K and V: each buffer
+              // is refilled once the previous item's last S MMA on it has
+              // completed, which is after that item's last K arrived
+              for (int t = 0; t < 2 && ok; ++t) {
+                if (q_issued[t] > 0)
+                  ok = mbar_wait(bar(kBarQEmpty + t), (q_issued[t] - 1) & 1, abort_flag, kRoleLoad, 90 + t);
+                if (!ok) break;
+                mbar_expect_tx(bar(kBarQFull + t), kTileBytes);
+                for (int x = 0; x < 2; ++x)
+                  tma_load_4d(sbase + kOffQ + t * kTileBytes + x * kBoxBytes, &tm_q, bar(kBarQFull + t), x * 64,
+                              m0 + t * 128, h, b);
+                q_issued[t]++;
+              }
+            }
+          }
         }
       }
       if (*abort_flag) {
         // drain: let every issued copy land before the CTA can exit
-        mbar_wait_drain(bar(kBarQFull), 0);
+        for (int t = 0; t < 2; ++t)
+          if (q_issued[t] > 0) mbar_wait_drain(bar(kBarQFull + t), (q_issued[t] - 1) & 1);
         for (int s = 0; s < kKvSlots; ++s)
           if (issued[s] > 0) mbar_wait_drain(bar(kBarKvFull + s), (issued[s] - 1) & 1);
       }
@@ -190,8 +253,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       constexpr uint32_t idesc_pv = idesc_bf16(128, 128, 0, 1);
       const uint32_t sQ = sbase + kOffQ;
       const uint32_t sKV = sbase + kOffKV;
-      bool ok = mbar_wait_warp(bar(kBarQFull), 0, abort_flag, kRoleMma, 0);
-      tc_fence_after();
+      bool ok = true;
       int pv_phase[2] = {0, 0};
       auto issue_s = [&](int t, int slot_k) {
         const uint32_t d = tmem + (uint32_t)(t * 128);
@@ -224,31 +286,47 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         pv_phase[t]++;
         return r;
       };
-      for (int it = 0; it < n_blocks && ok; ++it) {
-        const int uk = 2 * it, slot_k = uk % kKvSlots;
-        ok = mbar_wait_warp(bar(kBarKvFull + slot_k), (uk / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_k);
-        if (!ok) break;
-        tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (it > 0) {
-            const int uv = 2 * (it - 1) + 1, slot_v = uv % kKvSlots;
-            if (t == 0) {
-              ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
-              if (!ok) break;
+      // One flat pipeline over the blocks of all this CTA's items: global
+      // block g issues PV_t(g-1) before S_t(g) for each tile, so the last PV
+      // of an item interleaves with the first QK^T of the next one.
+      int g = 0;          // blocks issued so far (K of block g = unit 2g, V = 2g+1)
+      int prev_it = 0;    // position of block g-1 within its item
+      int n_items_done = 0;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_items_done) {
+        for (int it = 0; it < n_blocks && ok; ++it, ++g) {
+          const int uk = 2 * g, slot_k = uk % kKvSlots;
+          ok = mbar_wait_warp(bar(kBarKvFull + slot_k), (uk / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_k);
+          if (!ok) break;
+          tc_fence_after();
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (g > 0) {
+              const int uv = 2 * (g - 1) + 1, slot_v = uv % kKvSlots;
+              if (t == 0) {
+                ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
+                if (!ok) break;
+              }
+              if (!(ok = issue_pv(t, slot_v, prev_it > 0))) break;
+              if (prev_it == n_blocks - 1) mma_commit_e(bar(kBarOFull + t));
+              if (t == 1) mma_commit_e(bar(kBarKvEmpty + slot_v));
             }
-            if (!(ok = issue_pv(t, slot_v, it - 1 > 0))) break;
-            if (t == 1) mma_commit_e(bar(kBarKvEmpty + slot_v));
+            if (it == 0) {
+              ok = mbar_wait_warp(bar(kBarQFull + t), (uint32_t)n_items_done & 1, abort_flag, kRoleMma, t);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_s(t, slot_k);
+            mma_commit_e(bar(kBarSFull + t));
+            if (it == n_blocks - 1) mma_commit_e(bar(kBarQEmpty + t));
           }
-          issue_s(t, slot_k);
-          mma_commit_e(bar(kBarSFull + t));
+          if (ok) mma_commit_e(bar(kBarKvEmpty + slot_k));
+          prev_it = it;
         }
-        if (ok) mma_commit_e(bar(kBarKvEmpty + slot_k));
       }
-      if (ok) {
-        const int uv = 2 * (n_blocks - 1) + 1, slot_v = uv % kKvSlots;
+      if (ok && g > 0) {
+        const int uv = 2 * (g - 1) + 1, slot_v = uv % kKvSlots;
         ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!(ok = issue_pv(t, slot_v, n_blocks - 1 > 0))) break;
+          if (!(ok = issue_pv(t, slot_v, prev_it > 0))) break;
           mma_commit_e(bar(kBarOFull + t));
         }
         if (ok) mma_commit_e(bar(kBarKvEmpty + slot_v));
@@ -269,80 +347,93 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     const float sl2 = p.scale_log2;
     const float thr = p.rescale_threshold;
     const int tail_valid = p.skv - (n_blocks - 1) * 128;  // 1..128
-    float m_s = -INFINITY;  // running reference max, in scaled log2 units
-    float l = 0.f;          // running row sum (relative to m_s)
     bool ok = true;
-    for (int it = 0; it < n_blocks; ++it) {
-      ok = mbar_wait(bar(kBarSFull + t), it & 1, abort_flag, role, 30 + t);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t s[4][32];
+    int s_waits = 0;     // S_t tiles consumed (SFull_t phase)
+    int n_items_done = 0;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_items_done) {
+      float m_s = -INFINITY;  // running reference max, in scaled log2 units
+      float l = 0.f;          // running row sum (relative to m_s)
+      for (int it = 0; it < n_blocks; ++it, ++s_waits) {
+        ok = mbar_wait(bar(kBarSFull + t), (uint32_t)s_waits & 1, abort_flag, role, 30 + t);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t s[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
-      tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
+        tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
-      if (it == 0 && tail_valid < 128) {
-        // first (ragged tail) block: keys past skv do not exist
+        for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
+        if (it == 0 && tail_valid < 128) {
+          // first (ragged tail) block: keys past skv do not exist
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
-      }
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          mx[i & 3] = fmax3(mx[i & 3], __uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1]));
-      const float mnew_s = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
-      if (it == 0) {
-        m_s = mnew_s;
-      } else {
-        // move the reference max only when the row max grew past the rescale
-        // threshold (exact by max-shift invariance; rare after a few blocks)
-        const bool need = mnew_s - m_s > thr;
-        if (__any_sync(0xffffffffu, need)) {
-          const float factor = need ? ex2_approx(m_s - mnew_s) : 1.f;
-          if (need) {
-            l *= factor;
-            m_s = mnew_s;
-          }
-          // O_t holds the sum through block it-1 (its PV completed before S_t(it) was signalled)
+          for (int i = 0; i < 16; ++i)
+            mx[i & 3] = fmax3(mx[i & 3], __uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1]));
+        const float mnew_s = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+        if (it == 0) {
+          m_s = mnew_s;
+        } else {
+          // move the reference max only when the row max grew past the rescale
+          // threshold (exact by max-shift invariance; rare after a few blocks)
+          const bool need = mnew_s - m_s > thr;
+          if (__any_sync(0xffffffffu, need)) {
+            const float factor = need ? ex2_approx(m_s - mnew_s) : 1.f;
+            if (need) {
+              l *= factor;
+              m_s = mnew_s;
+            }
+            // O_t holds the sum through block it-1 (its PV completed before S_t(it) was signalled)
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            uint32_t o[16];
-            tmem_ld16(tO + c * 16, o);
-            tmem_wait_ld();
-            reg_fence16(o);
+            for (int c = 0; c < 8; ++c) {
+              uint32_t o[16];
+              tmem_ld16(tO + c * 16, o);
+              tmem_wait_ld();
+              reg_fence16(o);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-            tmem_st16(tO + c * 16, o);
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+              tmem_st16(tO + c * 16, o);
+            }
           }
         }
+        // P in two halves: the PV MMA on keys 0-63 starts while keys 64-127
+        // are still being exponentiated.  The arrivals also tell the MMA warp
+        // that this item's O_t readout (the epilogue below, in program order
+        // before the next item's first P) is complete.
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negx2 = f2_pack(-m_s, -m_s);
+        float bsum = fwd_exp_half(s, 0, tS, sl2x2, negx2);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive_warp(bar(kBarPFull + 2 * t));
+        bsum += fwd_exp_half(s, 2, tS, sl2x2, negx2);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive_warp(bar(kBarPFull + 2 * t + 1));
+        l += bsum;
       }
-      // P in two halves: the PV MMA on keys 0-63 starts while keys 64-127
-      // are still being exponentiated
-      const uint64_t sl2x2 = f2_pack(sl2, sl2), negx2 = f2_pack(-m_s, -m_s);
-      float bsum = fwd_exp_half(s, 0, tS, sl2x2, negx2);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive_warp(bar(kBarPFull + 2 * t));
-      bsum += fwd_exp_half(s, 2, tS, sl2x2, negx2);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive_warp(bar(kBarPFull + 2 * t + 1));
-      l += bsum;
-    }
-    // ----------------------------------------------------------- epilogue
-    if (ok) ok = mbar_wait(bar(kBarOFull + t), 0, abort_flag, role, 40 + t);
-    if (ok) {
+      // --------------------------------------------------------- epilogue
+      if (ok) ok = mbar_wait(bar(kBarOFull + t), (uint32_t)n_items_done & 1, abort_flag, role, 40 + t);
+      if (!ok) break;
       tc_fence_after();
-      const int row = m0 + t * 128 + wq * 32 + lane;
-      const bool valid = row < p.sq;
+      int m0, h, b;
+      item_coords(item, m0, h, b);
+      const int r = wq * 32 + lane;  // row within the tile
+      const int row = m0 + t * 128 + r;
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.o + (((size_t)b * p.sq + (valid ? row : 0)) * p.h + h) * 128;
+      // O_t / l as bf16 into the stage (two 128B-swizzled boxes of 64
+      // columns, the tensor store's layout) once the previous tile's store
+      // has read it
+      const int use = 2 * n_items_done + t;
+      if (use > 0) ok = mbar_wait(bar(kBarOStageFree), (uint32_t)(use - 1) & 1, abort_flag, role, 45 + t);
+      if (!ok) break;
+      const uint32_t stage = sbase + kOffOStage + (uint32_t)r * 128u;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -353,13 +444,17 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        if (valid) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            st_global_v4(orow + c * 32 + v * 8, pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        for (int v = 0; v < 4; ++v) {
+          const uint32_t chunk = (uint32_t)((c & 1) * 4 + v);  // 16-byte chunk within the 64-column box
+          st_shared_v4(stage + (uint32_t)(c >> 1) * kBoxBytes + ((chunk ^ ((uint32_t)r & 7u)) << 4), pk[4 * v],
+                       pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
       }
-      if (valid) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kBarOStaged));
+      if (row < p.sq) {
         // natural-log LSE; -inf when the row sum is zero or not finite
         const float lse = (l > 0.f && l == l) ? (m_s + log2f(l)) * 0.69314718055994531f : -INFINITY;
         p.lse[((size_t)b * p.h + h) * p.sq + row] = lse;

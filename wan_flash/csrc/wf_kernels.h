@@ -14,6 +14,8 @@ struct FwdParams {
   float* lse;
   int sq, skv, h;
   int n_blocks;            // ceil(skv / 128)
+  int n_pairs;             // ceil(sq / 256): work items per (batch, head)
+  int n_items;             // b * h * n_pairs
   float scale_log2;        // log2(e) / sqrt(128)
   float rescale_threshold; // log2 units
 };
@@ -37,7 +39,8 @@ struct BwdParams {
 };
 
 __global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                              const __grid_constant__ CUtensorMap tm_v, FwdParams p);
+                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                              FwdParams p);
 __global__ void wf_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                                    BwdParams p);
@@ -60,6 +63,9 @@ size_t bwd2_smem_bytes();
 constexpr bool kBwdPairDefault = false;
 
 constexpr int kFwdThreads = 384;
+// wf_fwd with scheduler = 0 (auto): persistent grid when KV has at most this
+// many 128-key blocks.
+constexpr int kFwdPersistMaxBlocks = 8;
 constexpr int kBwdThreads = 512;
 
 }  // namespace wf

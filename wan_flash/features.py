@@ -7,9 +7,14 @@ Forward flags
                           at most this many log2 units (exact by max-shift
                           invariance; only rounding differs).  0.0 = always
                           rescale.
-  scheduler               "auto" | "single" | "persistent".  This build has the
-                          one-CTA-per-tile grid; "persistent" is accepted and
-                          currently launches the same grid.
+  scheduler               "auto" | "single" | "persistent".  "single": one CTA
+                          per 256-row work item.  "persistent": one CTA per
+                          SM looping over the items, so the next item's Q
+                          load and first QK^T overlap the current item's
+                          last blocks and epilogue.  "auto": persistent
+                          when KV has at most 8 blocks of 128 keys (the
+                          cross-attention shapes), else single.
+  num_sms                 persistent grid size; 0 = the device's SM count.
   tile_m / tile_n         fixed at 128 x 128 (two 128-row query tiles per CTA).
   num_stages              K/V ring depth in (K, V) pairs (fixed at 2).
   cluster_mn              (1, 1) only: no TMA multicast anywhere (multi-GPU
@@ -54,6 +59,7 @@ class FwdFeatures:
     tile_n: int = 128
     scheduler: str = "auto"
     cluster_mn: tuple = (1, 1)
+    num_sms: int = 0
 
 
 @dataclass(frozen=True)
@@ -79,6 +85,8 @@ def _validate_fwd(f: FwdFeatures):
         raise ValueError("cluster_mn must be (1, 1): this build issues no multicast TMA loads")
     if f.scheduler not in ("auto", "single", "persistent"):
         raise ValueError(f"unknown scheduler {f.scheduler!r}")
+    if f.num_sms < 0:
+        raise ValueError("num_sms must be >= 0 (0 = the device's SM count)")
     if not (f.rescale_skip_threshold >= 0.0):
         raise ValueError("rescale_skip_threshold must be >= 0")
     if not f.intra_wg_overlap or not f.mma_pv_is_rs:

@@ -86,7 +86,8 @@ def _fwd_impl(q, k, v, marks=None):
         return o, lse
 
     f = features.get()
-    cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler], 0)
+    cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler],
+                      int(f.num_sms))
     with torch.cuda.device(q.device):
         _mark(marks, "fwd")
         rc = _lib.lib().wf_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), b, sq, skv, h,
