@@ -48,7 +48,7 @@ typedef enum wf_status {
 typedef struct wf_fwd_cfg {
   float rescale_threshold; /* skip the O rescale while the running max grew
                               by <= this many log2 units; 0 = always rescale */
-  int scheduler;           /* 0 = auto (persistent when skv <= 1024),
+  int scheduler;           /* 0 = auto (persistent when skv <= 8192),
                               1 = one CTA per 256-row work item,
                               2 = persistent (min(items, num_sms) CTAs)      */
   int num_sms;             /* persistent grid size; 0 = the device's SMs     */

@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
             const int i = 2 * v + e;
             const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2,
                                       e ? f2_pack(L.z, L.w) : f2_pack(L.x, L.y));
-            pp[c][i] = (kBwdPolyEvery > 0 && (i % kBwdPolyEvery) == kBwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
+            pp[c][i] = (kBwdPolyEvery > 0 && (i % (kBwdPolyEvery > 0 ? kBwdPolyEvery : 1)) == kBwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
             float p0, p1;
             f2_unpack(pp[c][i], p0, p1);
             pk[i] = kv_valid ? pack_bf16(p0, p1) : 0u;

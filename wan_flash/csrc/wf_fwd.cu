@@ -96,7 +96,7 @@ __device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0
     for (int i = 0; i < 16; ++i) {
       const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2, negx2);
       const uint64_t pp =
-          (kFwdPolyEvery > 0 && (i % kFwdPolyEvery) == kFwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
+          (kFwdPolyEvery > 0 && (i % (kFwdPolyEvery > 0 ? kFwdPolyEvery : 1)) == kFwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
       acc[i & 3] = f2_add(acc[i & 3], pp);
       float p0, p1;
       f2_unpack(pp, p0, p1);

@@ -65,7 +65,7 @@ constexpr bool kBwdPairDefault = false;
 constexpr int kFwdThreads = 384;
 // wf_fwd with scheduler = 0 (auto): persistent grid when KV has at most this
 // many 128-key blocks.
-constexpr int kFwdPersistMaxBlocks = 8;
+constexpr int kFwdPersistMaxBlocks = 64;
 constexpr int kBwdThreads = 512;
 
 }  // namespace wf

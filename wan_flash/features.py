@@ -12,8 +12,10 @@ Forward flags
                           SM looping over the items, so the next item's Q
                           load and first QK^T overlap the current item's
                           last blocks and epilogue.  "auto": persistent
-                          when KV has at most 8 blocks of 128 keys (the
-                          cross-attention shapes), else single.
+                          when KV has at most 64 blocks of 128 keys (cross
+                          attention and short self attention), else single
+                          (the hardware's dynamic CTA placement balances
+                          long items better than a static stride).
   num_sms                 persistent grid size; 0 = the device's SM count.
   tile_m / tile_n         fixed at 128 x 128 (two 128-row query tiles per CTA).
   num_stages              K/V ring depth in (K, V) pairs (fixed at 2).
