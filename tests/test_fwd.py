@@ -29,9 +29,10 @@ FAST_SHAPES = [
     WanShape("cross", 1, 2, 2048, 257),    # I2V image branch length
 ]
 
-# tile edges of the 256-row CTA / 128-row KV block
+# tile edges of the 256-row work item / 128-row KV block; KV tails of at most
+# 64 keys (1, 2, 16, 44, 63, 64) run the 64-key-wide tail block
 EDGE_SHAPES = [(1, 1), (1, 130), (63, 63), (64, 65), (127, 129), (128, 128), (129, 127), (255, 257), (256, 256),
-               (257, 300), (385, 1)]
+               (257, 300), (385, 1), (300, 192), (300, 193), (300, 64), (700, 16)]
 
 
 def _run(shape: WanShape, seed=0, std=1.0):

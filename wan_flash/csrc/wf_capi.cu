@@ -77,8 +77,10 @@ int device_setup(int* dev_out) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (major != 10 || minor != 0)
     return fail(WF_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major, minor);
-  e = cudaFuncSetAttribute(wf_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
+  e = cudaFuncSetAttribute(wf_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd smem)");
+  e = cudaFuncSetAttribute(wf_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd narrow smem)");
   e = cudaFuncSetAttribute(wf_bwd_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd smem)");
   e = cudaFuncSetAttribute(wf_bwd2_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd2_smem_bytes());
@@ -234,7 +236,11 @@ int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
   const int sms = (cfg && cfg->num_sms > 0) ? cfg->num_sms : g_dev_sms[dev];
   const bool persistent = sched == 2 || (sched == 0 && p.n_blocks <= kFwdPersistMaxBlocks);
   const int grid = persistent ? (int)std::min<long long>(n_items, sms) : p.n_items;
-  wf_fwd_kernel<<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
+  const bool narrow_tail = skv - (p.n_blocks - 1) * 128 <= 64;
+  if (narrow_tail)
+    wf_fwd_kernel<true><<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
+  else
+    wf_fwd_kernel<false><<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
   return launch_check("wf_fwd launch");
 }
 

@@ -109,6 +109,10 @@ __device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0
   return a0 + a1;
 }
 
+// kNarrowTail: the ragged KV tail holds at most 64 keys and runs as a
+// 64-key block (a separate instantiation, so the steady-state blocks of the
+// common case carry none of it).
+template <bool kNarrowTail>
 __global__ void __launch_bounds__(fwd::kThreads, 1)
     wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -250,26 +254,32 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     // ------------------------------------------------------------------ MMA
     {  // converged warp: all lanes wait and form descriptors, elected lanes issue
       constexpr uint32_t idesc_qk = idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_qk_narrow = idesc_bf16(128, 64, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16(128, 128, 0, 1);
+      // a ragged tail of at most 64 keys (e.g. 257 = 2 x 128 + 1) runs as a
+      // 64-key block: QK^T with N = 64 and PV over keys 0-63 only
+      constexpr bool narrow_tail = kNarrowTail;
       const uint32_t sQ = sbase + kOffQ;
       const uint32_t sKV = sbase + kOffKV;
       bool ok = true;
       int pv_phase[2] = {0, 0};
-      auto issue_s = [&](int t, int slot_k) {
+      auto issue_s = [&](int t, int slot_k, bool narrow) {
         const uint32_t d = tmem + (uint32_t)(t * 128);
         const uint64_t a0 = sdesc(sQ + t * kTileBytes, 16, 1024);
         const uint64_t b0 = sdesc(sKV + slot_k * kTileBytes, 16, 1024);
+        const uint32_t idesc = narrow ? idesc_qk_narrow : idesc_qk;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t off = (uint32_t)((ks >> 2) * kBoxBytes + (ks & 3) * 32);
-          mma_ss_e(d, desc_add(a0, off), desc_add(b0, off), idesc_qk, ks > 0);
+          mma_ss_e(d, desc_add(a0, off), desc_add(b0, off), idesc, ks > 0);
         }
       };
       // O_t += P_t V over keys [64*half, 64*half + 64) once that half of P_t
       // has been written (P_t: bf16 pairs in S_t columns [0, 64))
-      auto issue_pv_half = [&](int t, int half, int slot_v, bool acc) -> bool {
+      auto issue_pv_half = [&](int t, int half, int slot_v, bool acc, bool narrow) -> bool {
         if (!mbar_wait_warp(bar(kBarPFull + 2 * t + half), (uint32_t)pv_phase[t] & 1, abort_flag, kRoleMma, 20 + 2 * t + half))
           return false;
+        if (narrow && half == 1) return true;  // keys 64-127 of a narrow tail do not exist
         tc_fence_after();
         const uint32_t d = tmem + 256u + (uint32_t)(t * 128);
         const uint32_t a = tmem + (uint32_t)(t * 128);
@@ -281,8 +291,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         }
         return true;
       };
-      auto issue_pv = [&](int t, int slot_v, bool acc) -> bool {
-        const bool r = issue_pv_half(t, 0, slot_v, acc) && issue_pv_half(t, 1, slot_v, acc);
+      auto issue_pv = [&](int t, int slot_v, bool acc, bool narrow) -> bool {
+        const bool r = issue_pv_half(t, 0, slot_v, acc, narrow) && issue_pv_half(t, 1, slot_v, acc, narrow);
         pv_phase[t]++;
         return r;
       };
@@ -305,7 +315,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
                 ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
                 if (!ok) break;
               }
-              if (!(ok = issue_pv(t, slot_v, prev_it > 0))) break;
+              if (!(ok = issue_pv(t, slot_v, prev_it > 0, prev_it == 0 && narrow_tail))) break;
               if (prev_it == n_blocks - 1) mma_commit_e(bar(kBarOFull + t));
               if (t == 1) mma_commit_e(bar(kBarKvEmpty + slot_v));
             }
@@ -314,7 +324,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
               if (!ok) break;
               tc_fence_after();
             }
-            issue_s(t, slot_k);
+            issue_s(t, slot_k, it == 0 && narrow_tail);
             mma_commit_e(bar(kBarSFull + t));
             if (it == n_blocks - 1) mma_commit_e(bar(kBarQEmpty + t));
           }
@@ -326,7 +336,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         const int uv = 2 * (g - 1) + 1, slot_v = uv % kKvSlots;
         ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!(ok = issue_pv(t, slot_v, prev_it > 0))) break;
+          if (!(ok = issue_pv(t, slot_v, prev_it > 0, prev_it == 0 && narrow_tail))) break;
           mma_commit_e(bar(kBarOFull + t));
         }
         if (ok) mma_commit_e(bar(kBarKvEmpty + slot_v));
@@ -347,13 +357,48 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     const float sl2 = p.scale_log2;
     const float thr = p.rescale_threshold;
     const int tail_valid = p.skv - (n_blocks - 1) * 128;  // 1..128
+    constexpr bool narrow_tail = kNarrowTail;              // the tail block is 64 keys wide
     bool ok = true;
     int s_waits = 0;     // S_t tiles consumed (SFull_t phase)
     int n_items_done = 0;
     for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_items_done) {
       float m_s = -INFINITY;  // running reference max, in scaled log2 units
       float l = 0.f;          // running row sum (relative to m_s)
-      for (int it = 0; it < n_blocks; ++it, ++s_waits) {
+      int it0 = 0;
+      if constexpr (narrow_tail) {
+        // the ragged tail holds at most 64 keys: S columns 0-63 only, one P
+        // half (the MMA warp skips PV over keys 64-127)
+        ok = mbar_wait(bar(kBarSFull + t), (uint32_t)s_waits & 1, abort_flag, role, 30 + t);
+        if (!ok) break;
+        ++s_waits;
+        tc_fence_after();
+        uint32_t s[4][32];
+        tmem_ld32(tS, s[0]);
+        tmem_ld32(tS + 32, s[1]);
+        tmem_wait_ld();
+        reg_fence32(s[0]);
+        reg_fence32(s[1]);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i >= tail_valid) s[c][i] = __float_as_uint(-INFINITY);
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            mx[i & 1] = fmax3(mx[i & 1], __uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1]));
+        m_s = fmaxf(mx[0], mx[1]) * sl2;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negx2 = f2_pack(-m_s, -m_s);
+        l = fwd_exp_half(s, 0, tS, sl2x2, negx2);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive_warp(bar(kBarPFull + 2 * t));
+        mbar_arrive_warp(bar(kBarPFull + 2 * t + 1));
+        it0 = 1;
+      }
+      for (int it = it0; it < n_blocks; ++it, ++s_waits) {
         ok = mbar_wait(bar(kBarSFull + t), (uint32_t)s_waits & 1, abort_flag, role, 30 + t);
         if (!ok) break;
         tc_fence_after();
@@ -468,5 +513,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   tc_fence_after();
   if (warp == 8) tmem_dealloc(tmem, 512);
 }
+
+template __global__ void wf_fwd_kernel<false>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
+                                               const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
+                                               FwdParams);
+template __global__ void wf_fwd_kernel<true>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
+                                              const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
+                                              FwdParams);
 
 }  // namespace wf

@@ -38,6 +38,7 @@ struct BwdParams {
   int deterministic;
 };
 
+template <bool kNarrowTail>
 __global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                               FwdParams p);
