@@ -54,6 +54,10 @@ CONFIGS = {
     "c2": ("self", 1, 32760, 32760, 12, 1, "Wan2.1-1.3B 480p self-attention fwd+bwd (b=1, s=32760, h=12, d=128)"),
     "c3": ("cross", 1, 75600, 512, 12, 2, "Wan2.1 cross-attention fwd+bwd (sq=75600, skv=512, h=12)"),
     "c3i2v": ("cross", 1, 75600, 257, 12, 2, "Wan2.1 I2V image cross-attention fwd+bwd (sq=75600, skv=257, h=12)"),
+    # the I2V block's two cross attentions with the same Q (text 512 + image 257), one
+    # two-context launch forward and a shared dQ accumulator backward; kv_len is the text context
+    "c3dual": ("dual", 1, 75600, 512, 12, 2, "Wan2.1 I2V cross-attention, text (skv=512) + image (skv=257) "
+               "contexts of the same Q, fwd+bwd (sq=75600, h=12)"),
     "c4": ("self", 1, 75600, 75600, 40, 3, "Wan2.1-14B 720p self-attention fwd+bwd, head-sharded (b=1, s=75600, h=40)"),
     # the sequence-parallel block: self-attention over 75600 tokens plus cross-attention against
     # a 512-token context, activations sequence-sharded; the CPU arm samples its self-attention part
@@ -61,6 +65,7 @@ CONFIGS = {
            "self (75600) + cross (512) attention fwd+bwd, all-to-all back (b=1, h=40)"),
 }
 C5_CONTEXT = 512
+DUAL_IMAGE_CONTEXT = 257
 METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/4/8-GPU"
 # DRAM bytes (read + write) per launch per head, from one ncu capture of the
 # C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd_c2_h4.md);
@@ -158,8 +163,9 @@ class CpuSampler:
 
         self.kind, self.b, self.sq, self.skv, self.h, seed, _ = CONFIGS[cfg_name]
         self.rng = np.random.default_rng(seed)
-        self.k = round_bf16(self.rng.standard_normal((1, 1, self.skv, 128), dtype=np.float32))
-        self.v = round_bf16(self.rng.standard_normal((1, 1, self.skv, 128), dtype=np.float32))
+        lens = [self.skv] + ([DUAL_IMAGE_CONTEXT] if self.kind == "dual" else [])
+        self.kv = [tuple(round_bf16(self.rng.standard_normal((1, 1, n, 128), dtype=np.float32)) for _ in range(2))
+                   for n in lens]
 
     def run(self, rows: int) -> float:
         from oracle.oracle import oracle_bwd, oracle_fwd, round_bf16
@@ -169,8 +175,9 @@ class CpuSampler:
         q = round_bf16(self.rng.standard_normal((1, 1, rows, 128), dtype=np.float32))
         do = round_bf16(self.rng.standard_normal((1, 1, rows, 128), dtype=np.float32))
         t0 = time.perf_counter()
-        o, lse = oracle_fwd(q, self.k, self.v)
-        oracle_bwd(q, self.k, self.v, o, lse, do)
+        for k, v in self.kv:
+            o, lse = oracle_fwd(q, k, v)
+            oracle_bwd(q, k, v, o, lse, do)
         return time.perf_counter() - t0
 
     def rows_for(self, seconds: float) -> int:
@@ -179,8 +186,7 @@ class CpuSampler:
         return max(256, min(self.sq, rows))
 
     def flops(self, rows: int) -> float:
-        f, fb = flops(1, 1, rows, self.skv)
-        return f + fb
+        return sum(sum(flops(1, 1, rows, k.shape[2])) for k, _ in self.kv)
 
 
 def cpu_sample(cfg_name: str, target_s: float = 12.0):
@@ -192,8 +198,9 @@ def cpu_sample(cfg_name: str, target_s: float = 12.0):
         "unit": "TFLOP/s",
         "cores": _cpu_threads(),
         "kind": "port",
-        "sample": (f"oracle/oracle.py fp32 fwd+bwd on head 0: {rows} of {s.sq} query rows x {s.skv} keys "
-                   f"({dt:.1f} s); cost is linear in rows and heads"),
+        "sample": (f"oracle/oracle.py fp32 fwd+bwd on head 0: {rows} of {s.sq} query rows x "
+                   f"{' + '.join(str(k.shape[2]) for k, _ in s.kv)} keys ({dt:.1f} s); cost is linear in rows "
+                   f"and heads"),
     }
 
 
@@ -356,14 +363,16 @@ def main():
             value = sampler.flops(rows) * args.steps / t / 1e12
             cpu = {"value": value, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port",
                    "sample": (f"per step: oracle/oracle.py fp32 fwd+bwd on head 0, {rows} of {sq} query rows x "
-                              f"{skv} keys; cost is linear in rows and heads")}
+                              f"{' + '.join(str(kk.shape[2]) for kk, _ in sampler.kv)} keys; cost is linear in rows "
+                              f"and heads")}
             line = {
                 "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True,
                 "scaling": "weak" if args.config != "c4" else "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded)",
-                "config": {"workload": desc, "global_batch": b, "seq_len": sq, "kv_len": skv,
+                "config": {"workload": desc, "global_batch": b, "seq_len": sq,
+                           "kv_len": [skv, DUAL_IMAGE_CONTEXT] if kind == "dual" else skv,
                            "heads": h_total, "parallelism": "host cores"},
                 "cpu_baseline": cpu,
                 "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -410,9 +419,20 @@ def main():
 
     q, k, v, do = rnd(sq), rnd(skv), rnd(skv), rnd(sq)
     f_fwd, f_bwd = flops(b, h, sq, skv)
+    dual = kind == "dual"
+    if dual:
+        # the image context: same Q, separate softmax; FLOPs of both contexts
+        k1, v1 = rnd(DUAL_IMAGE_CONTEXT), rnd(DUAL_IMAGE_CONTEXT)
+        f1, fb1 = flops(b, h, sq, DUAL_IMAGE_CONTEXT)
+        f_fwd, f_bwd = f_fwd + f1, f_bwd + fb1
     step_flops = f_fwd + f_bwd
 
     def step(marks=None):
+        if dual:
+            interface._mark(marks, "fwd")
+            o0, lse0, o1, lse1 = interface.wan_flash_fwd_dual(q, k, v, k1, v1)
+            dq, grads = interface._bwd_multi(q, ((k, v, o0, lse0), (k1, v1, o1, lse1)), do, marks)
+            return o0, dq, grads
         o, lse = interface._fwd_impl(q, k, v, marks)
         dq, dk, dv = interface._bwd_impl(q, k, v, o, lse, do, marks)
         return o, dq, dk, dv
@@ -468,13 +488,15 @@ def main():
     # kernels run, as in a training input pipeline.
     e2e = None
     if not args.no_e2e:
-        from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+        from wan_flash.interface import wan_flash_bwd, wan_flash_bwd_dual, wan_flash_fwd, wan_flash_fwd_dual
 
-        hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
-        n_out = 4
-        host_out = [[torch.empty(t.shape, dtype=torch.bfloat16, pin_memory=True) for t in (q, q, k, v)]
+        ins = (q, k, v, do) + ((k1, v1) if dual else ())
+        hins = [t.cpu().pin_memory() for t in ins]
+        outs_like = (q, q, k, v) + ((k1, v1) if dual else ())
+        n_out = len(outs_like)
+        host_out = [[torch.empty(t.shape, dtype=torch.bfloat16, pin_memory=True) for t in outs_like]
                     for _ in range(2)]
-        dev_in = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+        dev_in = [[torch.empty_like(t) for t in ins] for _ in range(2)]
         dev_out = [[None] * n_out for _ in range(2)]
         copy_stream = torch.cuda.Stream(device=dev)  # host -> device
         read_stream = torch.cuda.Stream(device=dev)  # device -> host (the other PCIe direction)
@@ -489,15 +511,21 @@ def main():
             sl = i % 2
             with torch.cuda.stream(copy_stream):
                 copy_stream.wait_event(out_ready[sl])  # kernels of step i-2 are done with this set
-                for dst, src in zip(dev_in[sl], (hq, hk, hv, hdo)):
+                for dst, src in zip(dev_in[sl], hins):
                     dst.copy_(src, non_blocking=True)
                 in_ready[sl].record(copy_stream)
             compute_stream.wait_event(in_ready[sl])
             compute_stream.wait_event(out_read[sl])  # step i-2's results have been read back
-            qd, kd, vd, dod = dev_in[sl]
-            o_, lse_ = wan_flash_fwd(qd, kd, vd)
-            dq_, dk_, dv_ = wan_flash_bwd(qd, kd, vd, o_, lse_, dod)
-            dev_out[sl] = [o_, dq_, dk_, dv_]
+            if dual:
+                qd, kd, vd, dod, k1d, v1d = dev_in[sl]
+                o0_, lse0_, o1_, lse1_ = wan_flash_fwd_dual(qd, kd, vd, k1d, v1d)
+                dq_, dk_, dv_, dk1_, dv1_ = wan_flash_bwd_dual(qd, kd, vd, k1d, v1d, o0_, lse0_, o1_, lse1_, dod)
+                dev_out[sl] = [o0_ + o1_, dq_, dk_, dv_, dk1_, dv1_]
+            else:
+                qd, kd, vd, dod = dev_in[sl]
+                o_, lse_ = wan_flash_fwd(qd, kd, vd)
+                dq_, dk_, dv_ = wan_flash_bwd(qd, kd, vd, o_, lse_, dod)
+                dev_out[sl] = [o_, dq_, dk_, dv_]
             out_ready[sl].record(compute_stream)
             with torch.cuda.stream(read_stream):
                 read_stream.wait_event(out_ready[sl])
@@ -517,7 +545,7 @@ def main():
         e1.record(compute_stream)
         barrier()
         e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+        h2d = sum(t.numel() * t.element_size() for t in hins)
         d2h = sum(t.numel() * t.element_size() for t in host_out[0])
         e2e = {"value": step_flops * world / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -536,8 +564,12 @@ def main():
         dom_flops = f_bwd if dominant == "bwd_main" else f_fwd
         dom_ms = kern_ms[dominant]
         achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-        plan = interface.bwd_plan(b, sq, skv, h, torch.cuda.get_device_properties(dev).multi_processor_count)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        plan = interface.bwd_plan(b, sq, skv, h, sms)
         launches_per_step = 1 + 3 + (2 if plan["nsplit"] > 1 else 0)
+        if dual:  # one forward; a second preprocess and main; its own split-M converts
+            plan1 = interface.bwd_plan(b, sq, DUAL_IMAGE_CONTEXT, h, sms)
+            launches_per_step += 2 + (2 if plan1["nsplit"] > 1 else 0)
         cpu = None
         if not args.no_cpu and world == 1:
             cpu = cpu_sample(args.config)
@@ -555,7 +587,8 @@ def main():
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16; no dataset)",
             "config": {
-                "workload": desc, "global_batch": b, "seq_len": sq, "kv_len": skv, "heads_per_gpu": h,
+                "workload": desc, "global_batch": b, "seq_len": sq,
+                "kv_len": [skv, DUAL_IMAGE_CONTEXT] if dual else skv, "heads_per_gpu": h,
                 "heads_total": global_h, "head_dim": 128, "parallelism": f"heads/{world}",
                 "l2": "inputs larger than L2 (q/k/v/dO/o/grad working set >> 126 MB); no flush",
             },

@@ -80,13 +80,28 @@ int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
            int h, const wf_fwd_cfg* cfg, void* stream);
 
 /*
+ * Two-context forward (no reference counterpart; the Wan I2V cross
+ * attention, where the same query rows attend a text context and an image
+ * context and the model adds the two outputs): o_c = softmax(q k_c^T /
+ * sqrt(128)) v_c and lse_c for c = 0, 1 in one launch, each 256-row query
+ * block loaded once for both.  Same layouts as wf_fwd; each context's
+ * softmax, output and LSE are independent (o_0 and o_1 are what two wf_fwd
+ * calls would write, bitwise).
+ */
+int wf_fwd_dual(const void* q, const void* k0, const void* v0, const void* k1, const void* v1, void* o0, void* o1,
+                float* lse0, float* lse1, int b, int sq, int skv0, int skv1, int h, const wf_fwd_cfg* cfg,
+                void* stream);
+
+/*
  * Backward preprocess: dpsum = rowsum(o * dO) (fp32), neg_lse_log2 =
  * -lse * log2(e) (-inf on pad rows, lse == -inf mapped to 0; the reference's
  * lse_log2 workspace, negated), and zero dq_accum.
  * Replaces `compiled[0](*pre_args, stream)` of wan_flash/interface.py:190
  * (WanFlashBwdPreprocessSm90, wan_flash/bwd_sm90.py:99-235).
  *   dpsum, neg_lse_log2: (b, h, sq_rounded) fp32, sq_rounded = ceil(sq/128)*128
- *   dq_accum: b*h*sq_rounded*128 fp32 in 128-row tiles, see wf_bwd_convert
+ *   dq_accum: b*h*sq_rounded*128 fp32 in 128-row tiles, see wf_bwd_convert;
+ *   may be NULL (left untouched: the second KV context of a two-context
+ *   backward adds into the accumulator the first context's call zeroed)
  */
 int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* neg_lse_log2,
                float* dq_accum, int b, int sq, int sq_rounded, int h, void* stream);

@@ -28,7 +28,7 @@ STATUS_NAMES = {
 }
 
 EXPORTS = (
-    "wf_fwd", "wf_bwd_pre", "wf_bwd_main", "wf_bwd_convert", "wf_bwd_noalloc", "wf_last_error",
+    "wf_fwd", "wf_fwd_dual", "wf_bwd_pre", "wf_bwd_main", "wf_bwd_convert", "wf_bwd_noalloc", "wf_last_error",
     "wf_device_status", "wf_set_wait_limit_ns", "wf_selftest_wait_timeout", "wf_num_sms", "wf_version",
 )
 
@@ -52,6 +52,7 @@ def _declare(lib):
     vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
     fp = ctypes.POINTER(ctypes.c_float)
     lib.wf_fwd.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, ctypes.POINTER(FwdCfg), vp]
+    lib.wf_fwd_dual.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, i, ctypes.POINTER(FwdCfg), vp]
     lib.wf_bwd_pre.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]
     lib.wf_bwd_main.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, ctypes.POINTER(BwdCfg), vp]
     lib.wf_bwd_convert.argtypes = [vp, vp, f, i, i, i, vp]

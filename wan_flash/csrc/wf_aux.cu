@@ -67,7 +67,9 @@ __global__ void __launch_bounds__(256) wf_bwd_pre_kernel(const __nv_bfloat16* __
     }
   }
   // zero rows [row0, row0 + 64) of the tiled dQ accumulator: one 64-row half,
-  // a contiguous 32 KB run
+  // a contiguous 32 KB run (no accumulator: a second KV context's
+  // preprocess, adding into one the first context's call zeroed)
+  if (dq_accum == nullptr) return;
   const int m = row0 >> 7, half = (row0 >> 6) & 1;
   float4* run = reinterpret_cast<float4*>(dq_accum + (bh * (size_t)(sq_rounded >> 7) + m) * 16384 + half * 8192);
 #pragma unroll

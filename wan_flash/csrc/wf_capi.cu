@@ -77,10 +77,12 @@ int device_setup(int* dev_out) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (major != 10 || minor != 0)
     return fail(WF_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major, minor);
-  e = cudaFuncSetAttribute(wf_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
+  e = cudaFuncSetAttribute(wf_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd smem)");
-  e = cudaFuncSetAttribute(wf_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
+  e = cudaFuncSetAttribute(wf_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd narrow smem)");
+  e = cudaFuncSetAttribute(wf_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd dual smem)");
   e = cudaFuncSetAttribute(wf_bwd_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd smem)");
   e = cudaFuncSetAttribute(wf_bwd2_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd2_smem_bytes());
@@ -139,6 +141,70 @@ __global__ void wf_selftest_wait_kernel() {
   }
   __syncthreads();
   if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, 99u, 99u);
+}
+
+// Forward over one KV context, or two contexts attended by the same query
+// rows (each with its own softmax, output and LSE) in one launch.
+static int fwd_launch(const void* q, int n_ctx, const void* const* k, const void* const* v, void* const* o,
+                      float* const* lse, const int* skv, int b, int sq, int h, const wf_fwd_cfg* cfg,
+                      void* stream) {
+  int rc;
+  for (int c = 0; c < n_ctx; ++c)
+    if ((rc = check_dims(b, sq, skv[c], h))) return rc;
+  if (b == 0 || sq == 0 || h == 0) return WF_OK;
+  if (!q) return fail(WF_ERR_INVALID_ARG, "null pointer");
+  for (int c = 0; c < n_ctx; ++c) {
+    if (skv[c] == 0) return fail(WF_ERR_UNSUPPORTED, "skv == 0: attention over an empty key set");
+    if (!k[c] || !v[c] || !o[c] || !lse[c]) return fail(WF_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(q) || !aligned16(k[c]) || !aligned16(v[c]) || !aligned16(o[c]) ||
+        (reinterpret_cast<uintptr_t>(lse[c]) & 3))
+      return fail(WF_ERR_MISALIGNED, "q/k/v/o must be 16-byte aligned and lse 4-byte aligned");
+  }
+  int dev;
+  if ((rc = device_setup(&dev))) return rc;
+  CUtensorMap mq, mk[2], mv[2], mo[2];
+  if ((rc = make_bshd_map(&mq, q, b, sq, h))) return rc;
+  for (int c = 0; c < n_ctx; ++c)
+    if ((rc = make_bshd_map(&mk[c], k[c], b, skv[c], h)) || (rc = make_bshd_map(&mv[c], v[c], b, skv[c], h)) ||
+        (rc = make_bshd_map(&mo[c], o[c], b, sq, h)))
+      return rc;
+  if (n_ctx == 1) {  // the one-context kernels never read the second segment's maps
+    mk[1] = mk[0];
+    mv[1] = mv[0];
+    mo[1] = mo[0];
+  }
+  FwdParams p;
+  p.sq = sq;
+  p.h = h;
+  int total_blocks = 0;
+  for (int c = 0; c < 2; ++c) {
+    const int cc = c < n_ctx ? c : 0;
+    p.lse[c] = lse[cc];
+    p.skv[c] = skv[cc];
+    p.n_blocks[c] = (skv[cc] + 127) / 128;
+    if (c < n_ctx) total_blocks += p.n_blocks[c];
+  }
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  p.rescale_threshold = cfg ? cfg->rescale_threshold : 8.0f;
+  p.n_pairs = (sq + 255) / 256;
+  const long long n_items = (long long)p.n_pairs * h * b;
+  if (n_items > 0x7fffffffLL) return fail(WF_ERR_UNSUPPORTED, "%lld work items exceed the grid limit", n_items);
+  p.n_items = (int)n_items;
+  const int sched = cfg ? cfg->scheduler : 0;
+  if (sched < 0 || sched > 2) return fail(WF_ERR_INVALID_ARG, "scheduler %d not in {0, 1, 2}", sched);
+  if (cfg && cfg->num_sms < 0) return fail(WF_ERR_INVALID_ARG, "num_sms %d < 0", cfg->num_sms);
+  const int sms = (cfg && cfg->num_sms > 0) ? cfg->num_sms : g_dev_sms[dev];
+  const bool persistent = sched == 2 || (sched == 0 && total_blocks <= kFwdPersistMaxBlocks);
+  const int grid = persistent ? (int)std::min<long long>(n_items, sms) : p.n_items;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = fwd_smem_bytes();
+  if (n_ctx == 2)
+    wf_fwd_kernel<2><<<grid, kFwdThreads, smem, st>>>(mq, mk[0], mv[0], mo[0], mk[1], mv[1], mo[1], p);
+  else if (skv[0] - (p.n_blocks[0] - 1) * 128 <= 64)
+    wf_fwd_kernel<1><<<grid, kFwdThreads, smem, st>>>(mq, mk[0], mv[0], mo[0], mk[1], mv[1], mo[1], p);
+  else
+    wf_fwd_kernel<0><<<grid, kFwdThreads, smem, st>>>(mq, mk[0], mv[0], mo[0], mk[1], mv[1], mo[1], p);
+  return launch_check("wf_fwd launch");
 }
 
 }  // namespace wf
@@ -204,44 +270,23 @@ int wf_selftest_wait_timeout(unsigned long long limit_ns, unsigned int* info) {
 
 int wf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int b, int sq, int skv, int h,
            const wf_fwd_cfg* cfg, void* stream) {
-  int rc = check_dims(b, sq, skv, h);
-  if (rc) return rc;
-  if (b == 0 || sq == 0 || h == 0) return WF_OK;
-  if (skv == 0) return fail(WF_ERR_UNSUPPORTED, "skv == 0: attention over an empty key set");
-  if (!q || !k || !v || !o || !lse) return fail(WF_ERR_INVALID_ARG, "null pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (reinterpret_cast<uintptr_t>(lse) & 3))
-    return fail(WF_ERR_MISALIGNED, "q/k/v/o must be 16-byte aligned and lse 4-byte aligned");
-  int dev;
-  if ((rc = device_setup(&dev))) return rc;
-  CUtensorMap mq, mk, mv, mo;
-  if ((rc = make_bshd_map(&mq, q, b, sq, h)) || (rc = make_bshd_map(&mk, k, b, skv, h)) ||
-      (rc = make_bshd_map(&mv, v, b, skv, h)) || (rc = make_bshd_map(&mo, o, b, sq, h)))
-    return rc;
-  FwdParams p;
-  p.o = reinterpret_cast<__nv_bfloat16*>(o);
-  p.lse = lse;
-  p.sq = sq;
-  p.skv = skv;
-  p.h = h;
-  p.n_blocks = (skv + 127) / 128;
-  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
-  p.rescale_threshold = cfg ? cfg->rescale_threshold : 8.0f;
-  p.n_pairs = (sq + 255) / 256;
-  const long long n_items = (long long)p.n_pairs * h * b;
-  if (n_items > 0x7fffffffLL) return fail(WF_ERR_UNSUPPORTED, "%lld work items exceed the grid limit", n_items);
-  p.n_items = (int)n_items;
-  const int sched = cfg ? cfg->scheduler : 0;
-  if (sched < 0 || sched > 2) return fail(WF_ERR_INVALID_ARG, "scheduler %d not in {0, 1, 2}", sched);
-  if (cfg && cfg->num_sms < 0) return fail(WF_ERR_INVALID_ARG, "num_sms %d < 0", cfg->num_sms);
-  const int sms = (cfg && cfg->num_sms > 0) ? cfg->num_sms : g_dev_sms[dev];
-  const bool persistent = sched == 2 || (sched == 0 && p.n_blocks <= kFwdPersistMaxBlocks);
-  const int grid = persistent ? (int)std::min<long long>(n_items, sms) : p.n_items;
-  const bool narrow_tail = skv - (p.n_blocks - 1) * 128 <= 64;
-  if (narrow_tail)
-    wf_fwd_kernel<true><<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
-  else
-    wf_fwd_kernel<false><<<grid, kFwdThreads, fwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, mo, p);
-  return launch_check("wf_fwd launch");
+  const void* ks[1] = {k};
+  const void* vs[1] = {v};
+  void* os[1] = {o};
+  float* lses[1] = {lse};
+  const int skvs[1] = {skv};
+  return fwd_launch(q, 1, ks, vs, os, lses, skvs, b, sq, h, cfg, stream);
+}
+
+int wf_fwd_dual(const void* q, const void* k0, const void* v0, const void* k1, const void* v1, void* o0, void* o1,
+                float* lse0, float* lse1, int b, int sq, int skv0, int skv1, int h, const wf_fwd_cfg* cfg,
+                void* stream) {
+  const void* ks[2] = {k0, k1};
+  const void* vs[2] = {v0, v1};
+  void* os[2] = {o0, o1};
+  float* lses[2] = {lse0, lse1};
+  const int skvs[2] = {skv0, skv1};
+  return fwd_launch(q, 2, ks, vs, os, lses, skvs, b, sq, h, cfg, stream);
 }
 
 int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, float* neg_lse_log2, float* dq_accum, int b,
@@ -250,8 +295,9 @@ int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, fl
   if (rc) return rc;
   if (sq_rounded != (sq + 127) / 128 * 128) return fail(WF_ERR_INVALID_ARG, "sq_rounded must be ceil(sq/128)*128");
   if (b == 0 || sq == 0 || h == 0) return WF_OK;
-  if (!o || !dO || !lse || !dpsum || !neg_lse_log2 || !dq_accum) return fail(WF_ERR_INVALID_ARG, "null pointer");
-  if (!aligned16(o) || !aligned16(dO) || !aligned16(dpsum) || !aligned16(neg_lse_log2) || !aligned16(dq_accum))
+  if (!o || !dO || !lse || !dpsum || !neg_lse_log2) return fail(WF_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(o) || !aligned16(dO) || !aligned16(dpsum) || !aligned16(neg_lse_log2) ||
+      (dq_accum && !aligned16(dq_accum)))
     return fail(WF_ERR_MISALIGNED, "o/dO/dpsum/neg_lse_log2/dq_accum must be 16-byte aligned");
   int dev;
   if ((rc = device_setup(&dev))) return rc;

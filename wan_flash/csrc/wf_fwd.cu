@@ -109,15 +109,26 @@ __device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0
   return a0 + a1;
 }
 
-// kNarrowTail: the ragged KV tail holds at most 64 keys and runs as a
-// 64-key block (a separate instantiation, so the steady-state blocks of the
-// common case carry none of it).
-template <bool kNarrowTail>
+// kMode 0: one KV context; 1: one context whose ragged tail holds at most 64
+// keys and runs as a 64-key block; 2: two KV contexts (segments) attended
+// by the same query rows, each with its own softmax, output and LSE (the
+// Wan I2V text + image cross attention), tail width decided per segment.
+// Separate instantiations, so the common case carries none of the others.
+template <int kMode>
 __global__ void __launch_bounds__(fwd::kThreads, 1)
-    wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                  FwdParams p) {
+    wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k0,
+                  const __grid_constant__ CUtensorMap tm_v0, const __grid_constant__ CUtensorMap tm_o0,
+                  const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_v1,
+                  const __grid_constant__ CUtensorMap tm_o1, FwdParams p) {
   using namespace fwd;
+  constexpr int kSegs = (kMode == 2) ? 2 : 1;
+  // a segment whose ragged tail holds at most 64 keys runs it 64 keys wide
+  auto seg_narrow = [&](int seg) -> bool {
+    if constexpr (kMode == 2)
+      return p.skv[seg] - (p.n_blocks[seg] - 1) * 128 <= 64;
+    else
+      return kMode == 1;
+  };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -128,7 +139,6 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 
   const int warp = (int)warp_id();
   const int lane = (int)lane_id();
-  const int n_blocks = p.n_blocks;
   // work item = 256 query rows (two 128-row tiles) of one (batch, head);
   // item i covers rows 256 * (i % n_pairs) of head (i / n_pairs) % h
   auto item_coords = [&](int item, int& m0, int& h, int& b) {
@@ -178,20 +188,24 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     // buffer (item order, tile 0 first: the MMA completes O_0 of an item
     // before O_1, and O_1 before the next item's O_0).
     if (lane == 0) {
-      tma_prefetch_desc(&tm_o);
+      tma_prefetch_desc(&tm_o0);
+      if (kSegs > 1) tma_prefetch_desc(&tm_o1);
       int n = 0;  // tiles stored
       bool ok = true;
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
         int m0, h, b;
         item_coords(item, m0, h, b);
-        for (int t = 0; t < 2; ++t, ++n) {
-          ok = mbar_wait(bar(kBarOStaged), (uint32_t)n & 1, abort_flag, kRoleStore, 50 + t);
-          if (!ok) break;
-          for (int x = 0; x < 2; ++x)
-            tma_store_4d(&tm_o, sbase + kOffOStage + x * kBoxBytes, x * 64, m0 + t * 128, h, b);
-          bulk_commit_group();
-          bulk_wait_read_all();
-          mbar_arrive(bar(kBarOStageFree));
+        for (int seg = 0; seg < kSegs && ok; ++seg) {
+          const CUtensorMap* tm_o = seg ? &tm_o1 : &tm_o0;
+          for (int t = 0; t < 2; ++t, ++n) {
+            ok = mbar_wait(bar(kBarOStaged), (uint32_t)n & 1, abort_flag, kRoleStore, 50 + t);
+            if (!ok) break;
+            for (int x = 0; x < 2; ++x)
+              tma_store_4d(tm_o, sbase + kOffOStage + x * kBoxBytes, x * 64, m0 + t * 128, h, b);
+            bulk_commit_group();
+            bulk_wait_read_all();
+            mbar_arrive(bar(kBarOStageFree));
+          }
         }
       }
       bulk_wait_all();
@@ -201,8 +215,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_k0);
+      tma_prefetch_desc(&tm_v0);
+      if (kSegs > 1) {
+        tma_prefetch_desc(&tm_k1);
+        tma_prefetch_desc(&tm_v1);
+      }
       int q_issued[2] = {0, 0};                // Q loads per tile buffer
       int issued[kKvSlots] = {0, 0, 0, 0};     // K/V loads per ring slot
       int u = 0;                               // K/V units (K and V of a block alternate)
@@ -210,6 +228,10 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
         int m0, h, b;
         item_coords(item, m0, h, b);
+        for (int seg = 0; seg < kSegs && ok; ++seg) {
+        const int n_blocks = p.n_blocks[seg];
+        const CUtensorMap* tm_k = seg ? &tm_k1 : &tm_k0;
+        const CUtensorMap* tm_v = seg ? &tm_v1 : &tm_v0;
         for (int it = 0; it < n_blocks && ok; ++it) {
           const int j = (it == 0) ? (n_blocks - 1) : (it - 1);
           for (int kv = 0; kv < 2 && ok; ++kv, ++u) {  // 0 = K, 1 = V
@@ -218,12 +240,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
             if (use > 0) ok = mbar_wait(bar(kBarKvEmpty + slot), (use - 1) & 1, abort_flag, kRoleLoad, 100 + slot);
             if (!ok) break;
             mbar_expect_tx(bar(kBarKvFull + slot), kTileBytes);
-            const CUtensorMap* tm = kv ? &tm_v : &tm_k;
+            const CUtensorMap* tm = kv ? tm_v : tm_k;
             for (int x = 0; x < 2; ++x)
               tma_load_4d(sbase + kOffKV + slot * kTileBytes + x * kBoxBytes, tm, bar(kBarKvFull + slot),
                           x * 64, j * 128, h, b);
             issued[slot] = use + 1;
-            if (it == 0 && kv == 0) {
+            if (seg == 0 && it == 0 && kv == 0) {
               // the item's Q tiles go between its first K and V: each buffer
               // is refilled once the previous item's last S MMA on it has
               // completed, which is after that item's last K arrived
@@ -239,6 +261,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
               }
             }
           }
+        }
         }
       }
       if (*abort_flag) {
@@ -258,7 +281,6 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       constexpr uint32_t idesc_pv = idesc_bf16(128, 128, 0, 1);
       // a ragged tail of at most 64 keys (e.g. 257 = 2 x 128 + 1) runs as a
       // 64-key block: QK^T with N = 64 and PV over keys 0-63 only
-      constexpr bool narrow_tail = kNarrowTail;
       const uint32_t sQ = sbase + kOffQ;
       const uint32_t sKV = sbase + kOffKV;
       bool ok = true;
@@ -299,10 +321,15 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       // One flat pipeline over the blocks of all this CTA's items: global
       // block g issues PV_t(g-1) before S_t(g) for each tile, so the last PV
       // of an item interleaves with the first QK^T of the next one.
-      int g = 0;          // blocks issued so far (K of block g = unit 2g, V = 2g+1)
-      int prev_it = 0;    // position of block g-1 within its item
+      int g = 0;                 // blocks issued so far (K of block g = unit 2g, V = 2g+1)
+      int prev_it = 0;           // position of block g-1 within its segment
+      bool prev_last = false;    // block g-1 ends its segment: its PV completes O
+      bool prev_narrow = false;  // block g-1 is a 64-key-wide tail
       int n_items_done = 0;
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_items_done) {
+        for (int seg = 0; seg < kSegs && ok; ++seg) {
+        const int n_blocks = p.n_blocks[seg];
+        const bool narrow_tail = seg_narrow(seg);
         for (int it = 0; it < n_blocks && ok; ++it, ++g) {
           const int uk = 2 * g, slot_k = uk % kKvSlots;
           ok = mbar_wait_warp(bar(kBarKvFull + slot_k), (uk / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_k);
@@ -315,28 +342,31 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
                 ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
                 if (!ok) break;
               }
-              if (!(ok = issue_pv(t, slot_v, prev_it > 0, prev_it == 0 && narrow_tail))) break;
-              if (prev_it == n_blocks - 1) mma_commit_e(bar(kBarOFull + t));
+              if (!(ok = issue_pv(t, slot_v, prev_it > 0, prev_narrow))) break;
+              if (prev_last) mma_commit_e(bar(kBarOFull + t));
               if (t == 1) mma_commit_e(bar(kBarKvEmpty + slot_v));
             }
-            if (it == 0) {
+            if (seg == 0 && it == 0) {
               ok = mbar_wait_warp(bar(kBarQFull + t), (uint32_t)n_items_done & 1, abort_flag, kRoleMma, t);
               if (!ok) break;
               tc_fence_after();
             }
             issue_s(t, slot_k, it == 0 && narrow_tail);
             mma_commit_e(bar(kBarSFull + t));
-            if (it == n_blocks - 1) mma_commit_e(bar(kBarQEmpty + t));
+            if (seg == kSegs - 1 && it == n_blocks - 1) mma_commit_e(bar(kBarQEmpty + t));
           }
           if (ok) mma_commit_e(bar(kBarKvEmpty + slot_k));
           prev_it = it;
+          prev_last = (it == n_blocks - 1);
+          prev_narrow = (it == 0) && narrow_tail;
+        }
         }
       }
       if (ok && g > 0) {
         const int uv = 2 * (g - 1) + 1, slot_v = uv % kKvSlots;
         ok = mbar_wait_warp(bar(kBarKvFull + slot_v), (uv / kKvSlots) & 1, abort_flag, kRoleMma, 10 + slot_v);
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!(ok = issue_pv(t, slot_v, prev_it > 0, prev_it == 0 && narrow_tail))) break;
+          if (!(ok = issue_pv(t, slot_v, prev_it > 0, prev_narrow))) break;
           mma_commit_e(bar(kBarOFull + t));
         }
         if (ok) mma_commit_e(bar(kBarKvEmpty + slot_v));
@@ -356,16 +386,17 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     const uint32_t tO = tmem + lane_base + 256u + (uint32_t)(t * 128);
     const float sl2 = p.scale_log2;
     const float thr = p.rescale_threshold;
-    const int tail_valid = p.skv - (n_blocks - 1) * 128;  // 1..128
-    constexpr bool narrow_tail = kNarrowTail;              // the tail block is 64 keys wide
     bool ok = true;
     int s_waits = 0;     // S_t tiles consumed (SFull_t phase)
-    int n_items_done = 0;
-    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_items_done) {
+    int n_segs_done = 0;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+      for (int seg = 0; seg < kSegs && ok; ++seg, ++n_segs_done) {
+      const int n_blocks = p.n_blocks[seg];
+      const int tail_valid = p.skv[seg] - (n_blocks - 1) * 128;  // 1..128
       float m_s = -INFINITY;  // running reference max, in scaled log2 units
       float l = 0.f;          // running row sum (relative to m_s)
       int it0 = 0;
-      if constexpr (narrow_tail) {
+      if (kMode != 0 && seg_narrow(seg)) {
         // the ragged tail holds at most 64 keys: S columns 0-63 only, one P
         // half (the MMA warp skips PV over keys 64-127)
         ok = mbar_wait(bar(kBarSFull + t), (uint32_t)s_waits & 1, abort_flag, role, 30 + t);
@@ -464,7 +495,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         l += bsum;
       }
       // --------------------------------------------------------- epilogue
-      if (ok) ok = mbar_wait(bar(kBarOFull + t), (uint32_t)n_items_done & 1, abort_flag, role, 40 + t);
+      if (ok) ok = mbar_wait(bar(kBarOFull + t), (uint32_t)n_segs_done & 1, abort_flag, role, 40 + t);
       if (!ok) break;
       tc_fence_after();
       int m0, h, b;
@@ -475,7 +506,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       // O_t / l as bf16 into the stage (two 128B-swizzled boxes of 64
       // columns, the tensor store's layout) once the previous tile's store
       // has read it
-      const int use = 2 * n_items_done + t;
+      const int use = 2 * n_segs_done + t;
       if (use > 0) ok = mbar_wait(bar(kBarOStageFree), (uint32_t)(use - 1) & 1, abort_flag, role, 45 + t);
       if (!ok) break;
       const uint32_t stage = sbase + kOffOStage + (uint32_t)r * 128u;
@@ -502,7 +533,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       if (row < p.sq) {
         // natural-log LSE; -inf when the row sum is zero or not finite
         const float lse = (l > 0.f && l == l) ? (m_s + log2f(l)) * 0.69314718055994531f : -INFINITY;
-        p.lse[((size_t)b * p.h + h) * p.sq + row] = lse;
+        p.lse[seg][((size_t)b * p.h + h) * p.sq + row] = lse;
+      }
       }
     }
   }
@@ -514,11 +546,14 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   if (warp == 8) tmem_dealloc(tmem, 512);
 }
 
-template __global__ void wf_fwd_kernel<false>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                               const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                               FwdParams);
-template __global__ void wf_fwd_kernel<true>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                              const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                              FwdParams);
+#define WF_FWD_INSTANTIATE(MODE)                                                                            \
+  template __global__ void wf_fwd_kernel<MODE>(                                                                   \
+      const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap, \
+      const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap, \
+      const __grid_constant__ CUtensorMap, FwdParams);
+WF_FWD_INSTANTIATE(0)
+WF_FWD_INSTANTIATE(1)
+WF_FWD_INSTANTIATE(2)
+#undef WF_FWD_INSTANTIATE
 
 }  // namespace wf

@@ -10,10 +10,10 @@
 namespace wf {
 
 struct FwdParams {
-  __nv_bfloat16* o;
-  float* lse;
-  int sq, skv, h;
-  int n_blocks;            // ceil(skv / 128)
+  float* lse[2];           // per KV segment: (b, h, sq) natural-log LSE
+  int sq, h;
+  int skv[2];              // per KV segment (segment 1 only in the two-context kernel)
+  int n_blocks[2];         // ceil(skv / 128)
   int n_pairs;             // ceil(sq / 256): work items per (batch, head)
   int n_items;             // b * h * n_pairs
   float scale_log2;        // log2(e) / sqrt(128)
@@ -38,10 +38,11 @@ struct BwdParams {
   int deterministic;
 };
 
-template <bool kNarrowTail>
-__global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                              FwdParams p);
+template <int kMode>
+__global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k0,
+                              const __grid_constant__ CUtensorMap tm_v0, const __grid_constant__ CUtensorMap tm_o0,
+                              const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_v1,
+                              const __grid_constant__ CUtensorMap tm_o1, FwdParams p);
 __global__ void wf_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                                    BwdParams p);

@@ -153,61 +153,124 @@ def wan_flash_bwd(
 
 
 def _bwd_impl(q, k, v, o, lse, do, marks=None):
-    assert all(t.dtype == torch.bfloat16 for t in (q, k, v, o, do))
-    assert lse.dtype == torch.float32
+    dq, ((dk, dv),) = _bwd_multi(q, ((k, v, o, lse),), do, marks)
+    return dq, dk, dv
+
+
+def _bwd_multi(q, contexts, do, marks=None):
+    """Backward of sum_c attention(q, k_c, v_c) for one or two KV contexts
+    given o_c, lse_c of each and dO of the sum: the contexts' main kernels
+    add into one dQ accumulator (zeroed by the first preprocess), converted
+    once.  Returns (dq, ((dk_c, dv_c), ...))."""
+    assert do.dtype == torch.bfloat16 and q.dtype == torch.bfloat16 and do.shape == q.shape
     b, sq, h, d = q.shape
-    bk, skv, hk, dk_ = k.shape
-    assert (b, h, d) == (bk, hk, dk_) and v.shape == k.shape
-    assert o.shape == q.shape and do.shape == q.shape
-    assert lse.shape == (b, h, sq)
     assert d == 128, "specialized for head_dim=128"
-    assert all(t.is_cuda and t.device == q.device for t in (k, v, o, lse, do)), "tensors must be on one CUDA device"
-    q, k, v, o, do = (_aligned(t) for t in (q, k, v, o, do))
-    lse = lse if lse.is_contiguous() else lse.contiguous()
-
+    for k, v, o, lse in contexts:
+        assert all(t.dtype == torch.bfloat16 for t in (k, v, o))
+        assert lse.dtype == torch.float32
+        bk, skv, hk, dk_ = k.shape
+        assert (b, h, d) == (bk, hk, dk_) and v.shape == k.shape
+        assert o.shape == q.shape
+        assert lse.shape == (b, h, sq)
+        assert all(t.is_cuda and t.device == q.device for t in (k, v, o, lse, do)), \
+            "tensors must be on one CUDA device"
+    q, do = _aligned(q), _aligned(do)
     dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
-    if b == 0 or h == 0 or skv == 0:
-        return dq.zero_(), dk, dv
+    grads = [(torch.empty_like(k), torch.empty_like(v)) for k, v, _, _ in contexts]
+    live = [c for c, (k, _, _, _) in enumerate(contexts) if b > 0 and h > 0 and k.shape[1] > 0]
     if sq == 0:
-        return dq, dk.zero_(), dv.zero_()
+        for dk, dv in grads:
+            dk.zero_(), dv.zero_()
+        return dq, tuple(grads)
+    if not live:
+        return dq.zero_(), tuple(grads)
 
-    plan = bwd_plan(b, sq, skv, h, _sms(q.device))
-    sq_rounded, nsplit = plan["sq_rounded"], plan["nsplit"]
     dev = q.device
-    dpsum = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
-    neg_lse_log2 = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
+    sq_rounded = -(-sq // BWD_TILE_M) * BWD_TILE_M
     dq_accum = torch.empty(b, h, sq_rounded * d, device=dev, dtype=torch.float32)
-    if nsplit > 1:
-        # split-M: dK/dV accumulate in fp32 (must start zeroed)
-        dk_accum = torch.zeros(b, h, plan["skv_rounded"] * d, device=dev, dtype=torch.float32)
-        dv_accum = torch.zeros_like(dk_accum)
-        main_dk, main_dv = dk_accum, dv_accum
-    else:
-        main_dk, main_dv = dk, dv
-
     L = _lib.lib()
     stream = ctypes.c_void_p(_stream_ptr(dev))
-    cfg = _lib.BwdCfg(nsplit, plan["cluster_n"])
-    if plan["deterministic"]:
-        sem = torch.zeros(plan["sem_len"], device=dev, dtype=torch.int32)
-        cfg.deterministic, cfg.sem = 1, sem.data_ptr()
+    # per context: plan, workspaces, preprocess (the first one zeroes dq_accum)
+    runs = []
     with torch.cuda.device(dev):
         _mark(marks, "bwd_pre")
-        _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(neg_lse_log2), _ptr(dq_accum),
-                                b, sq, sq_rounded, h, stream))
+        for i, c in enumerate(live):
+            k, v, o, lse = contexts[c]
+            k, v, o = (_aligned(t) for t in (k, v, o))
+            lse = lse if lse.is_contiguous() else lse.contiguous()
+            skv = k.shape[1]
+            plan = bwd_plan(b, sq, skv, h, _sms(dev))
+            dpsum = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
+            neg_lse_log2 = torch.empty(b, h, sq_rounded, device=dev, dtype=torch.float32)
+            dk, dv = grads[c]
+            if plan["nsplit"] > 1:
+                # split-M: dK/dV accumulate in fp32 (must start zeroed)
+                dk_accum = torch.zeros(b, h, plan["skv_rounded"] * d, device=dev, dtype=torch.float32)
+                dv_accum = torch.zeros_like(dk_accum)
+            else:
+                dk_accum = dv_accum = None
+            cfg = _lib.BwdCfg(plan["nsplit"], plan["cluster_n"])
+            sem = None
+            if plan["deterministic"]:
+                sem = torch.zeros(plan["sem_len"], device=dev, dtype=torch.int32)
+                cfg.deterministic, cfg.sem = 1, sem.data_ptr()
+            _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(neg_lse_log2),
+                                    _ptr(dq_accum) if i == 0 else None, b, sq, sq_rounded, h, stream))
+            runs.append((k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, sem))
         _mark(marks, "bwd_main")
-        _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(neg_lse_log2), _ptr(dpsum),
-                                 _ptr(dq_accum), _ptr(main_dk), _ptr(main_dv), b, sq, skv, h,
-                                 ctypes.byref(cfg), stream))
+        for k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, _sem in runs:
+            main_dk = dk_accum if dk_accum is not None else dk
+            main_dv = dv_accum if dv_accum is not None else dv
+            _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(neg_lse_log2), _ptr(dpsum),
+                                     _ptr(dq_accum), _ptr(main_dk), _ptr(main_dv), b, sq, skv, h,
+                                     ctypes.byref(cfg), stream))
         _mark(marks, "bwd_convert")
         _lib.check(L.wf_bwd_convert(_ptr(dq_accum), _ptr(dq), ctypes.c_float(1.0 / math.sqrt(d)), b, sq, h, stream))
-        if nsplit > 1:
-            _lib.check(L.wf_bwd_convert(_ptr(dk_accum), _ptr(dk), ctypes.c_float(1.0), b, skv, h, stream))
-            _lib.check(L.wf_bwd_convert(_ptr(dv_accum), _ptr(dv), ctypes.c_float(1.0), b, skv, h, stream))
+        for k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, _sem in runs:
+            if dk_accum is not None:
+                _lib.check(L.wf_bwd_convert(_ptr(dk_accum), _ptr(dk), ctypes.c_float(1.0), b, skv, h, stream))
+                _lib.check(L.wf_bwd_convert(_ptr(dv_accum), _ptr(dv), ctypes.c_float(1.0), b, skv, h, stream))
         _mark(marks, "end")
-    return dq, dk, dv
+    return dq, tuple(grads)
+
+
+def wan_flash_fwd_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor):
+    """Two KV contexts attended by the same query rows in one launch (the Wan
+    I2V cross attention: a text context and an image context, whose outputs
+    the model adds).  Returns (o0, lse0, o1, lse1), each exactly what
+    wan_flash_fwd(q, k_c, v_c) returns; every 256-row query block is loaded
+    once for both contexts.  No reference counterpart."""
+    assert q.dtype == torch.bfloat16 and q.dim() == 4
+    b, sq, h, d = q.shape
+    assert d == 128, "specialized for head_dim=128"
+    for k, v in ((k0, v0), (k1, v1)):
+        assert k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16 and k.dim() == 4
+        assert (k.shape[0], k.shape[2], k.shape[3]) == (b, h, d) and v.shape == k.shape
+        assert q.is_cuda and k.device == q.device and v.device == q.device, "tensors must be on one CUDA device"
+        assert k.shape[1] > 0 or sq == 0 or b == 0 or h == 0, "attention over an empty key set"
+    q, k0, v0, k1, v1 = (_aligned(t) for t in (q, k0, v0, k1, v1))
+    o0, o1 = torch.empty_like(q), torch.empty_like(q)
+    lse0 = torch.empty(b, h, sq, device=q.device, dtype=torch.float32)
+    lse1 = torch.empty_like(lse0)
+    if o0.numel() == 0:
+        return o0, lse0, o1, lse1
+    f = features.get()
+    cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler],
+                      int(f.num_sms))
+    with torch.cuda.device(q.device):
+        rc = _lib.lib().wf_fwd_dual(_ptr(q), _ptr(k0), _ptr(v0), _ptr(k1), _ptr(v1), _ptr(o0), _ptr(o1),
+                                    _ptr(lse0), _ptr(lse1), b, sq, k0.shape[1], k1.shape[1], h,
+                                    ctypes.byref(cfg), ctypes.c_void_p(_stream_ptr(q.device)))
+    _lib.check(rc)
+    return o0, lse0, o1, lse1
+
+
+def wan_flash_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do):
+    """Backward of o0 + o1 (wan_flash_fwd_dual's outputs) given dO of the
+    sum: (dq, dk0, dv0, dk1, dv1).  Both contexts add into one dQ accumulator
+    that is zeroed and converted once."""
+    dq, ((dk0, dv0), (dk1, dv1)) = _bwd_multi(q, ((k0, v0, o0, lse0), (k1, v1, o1, lse1)), do)
+    return dq, dk0, dv0, dk1, dv1
 
 
 class _WanFlashAttnFn(torch.autograd.Function):
@@ -227,3 +290,21 @@ class _WanFlashAttnFn(torch.autograd.Function):
 def wan_flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     """Differentiable attention: our fwd + our bwd. Returns o (b,s,h,d) bf16."""
     return _WanFlashAttnFn.apply(q, k, v)
+
+
+class _WanFlashAttnDualFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k0, v0, k1, v1):
+        o0, lse0, o1, lse1 = wan_flash_fwd_dual(q, k0, v0, k1, v1)
+        ctx.save_for_backward(q, k0, v0, k1, v1, o0, lse0, o1, lse1)
+        return o0 + o1
+
+    @staticmethod
+    def backward(ctx, do):
+        return wan_flash_bwd_dual(*ctx.saved_tensors, do.contiguous())
+
+
+def wan_flash_attn_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor):
+    """Differentiable attention(q, k0, v0) + attention(q, k1, v1) (the Wan I2V
+    text + image cross attention) with the two-context kernels."""
+    return _WanFlashAttnDualFn.apply(q, k0, v0, k1, v1)
