@@ -121,11 +121,15 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
                   const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_v1,
                   const __grid_constant__ CUtensorMap tm_o1, FwdParams p) {
   using namespace fwd;
+  // Segment loops stay rolled and per-segment parameters are read with
+  // constant indices: an unrolled copy of the block loops, or the parameter
+  // arrays copied to local memory for a run-time index, each cost the
+  // two-context kernel 7-25 % against two one-context launches.
   constexpr int kSegs = (kMode == 2) ? 2 : 1;
   // a segment whose ragged tail holds at most 64 keys runs it 64 keys wide
   auto seg_narrow = [&](int seg) -> bool {
     if constexpr (kMode == 2)
-      return p.skv[seg] - (p.n_blocks[seg] - 1) * 128 <= 64;
+      return (seg ? p.skv[1] : p.skv[0]) - ((seg ? p.n_blocks[1] : p.n_blocks[0]) - 1) * 128 <= 64;
     else
       return kMode == 1;
   };
@@ -195,6 +199,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
         int m0, h, b;
         item_coords(item, m0, h, b);
+        #pragma unroll 1
         for (int seg = 0; seg < kSegs && ok; ++seg) {
           const CUtensorMap* tm_o = seg ? &tm_o1 : &tm_o0;
           for (int t = 0; t < 2; ++t, ++n) {
@@ -228,8 +233,9 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
         int m0, h, b;
         item_coords(item, m0, h, b);
+        #pragma unroll 1
         for (int seg = 0; seg < kSegs && ok; ++seg) {
-        const int n_blocks = p.n_blocks[seg];
+        const int n_blocks = (seg ? p.n_blocks[1] : p.n_blocks[0]);
         const CUtensorMap* tm_k = seg ? &tm_k1 : &tm_k0;
         const CUtensorMap* tm_v = seg ? &tm_v1 : &tm_v0;
         for (int it = 0; it < n_blocks && ok; ++it) {
@@ -327,8 +333,9 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       bool prev_narrow = false;  // block g-1 is a 64-key-wide tail
       int n_items_done = 0;
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++n_items_done) {
+        #pragma unroll 1
         for (int seg = 0; seg < kSegs && ok; ++seg) {
-        const int n_blocks = p.n_blocks[seg];
+        const int n_blocks = (seg ? p.n_blocks[1] : p.n_blocks[0]);
         const bool narrow_tail = seg_narrow(seg);
         for (int it = 0; it < n_blocks && ok; ++it, ++g) {
           const int uk = 2 * g, slot_k = uk % kKvSlots;
@@ -390,9 +397,10 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     int s_waits = 0;     // S_t tiles consumed (SFull_t phase)
     int n_segs_done = 0;
     for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+      #pragma unroll 1
       for (int seg = 0; seg < kSegs && ok; ++seg, ++n_segs_done) {
-      const int n_blocks = p.n_blocks[seg];
-      const int tail_valid = p.skv[seg] - (n_blocks - 1) * 128;  // 1..128
+      const int n_blocks = (seg ? p.n_blocks[1] : p.n_blocks[0]);
+      const int tail_valid = (seg ? p.skv[1] : p.skv[0]) - (n_blocks - 1) * 128;  // 1..128
       float m_s = -INFINITY;  // running reference max, in scaled log2 units
       float l = 0.f;          // running row sum (relative to m_s)
       int it0 = 0;
@@ -533,7 +541,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       if (row < p.sq) {
         // natural-log LSE; -inf when the row sum is zero or not finite
         const float lse = (l > 0.f && l == l) ? (m_s + log2f(l)) * 0.69314718055994531f : -INFINITY;
-        p.lse[seg][((size_t)b * p.h + h) * p.sq + row] = lse;
+        (seg ? p.lse[1] : p.lse[0])[((size_t)b * p.h + h) * p.sq + row] = lse;
       }
       }
     }
