@@ -63,3 +63,48 @@ def test_ops_match_interface_and_opcheck():
     wan_flash_attn(qb, kb, vb).backward(do)
     for a, b in zip((qa.grad, ka.grad, va.grad), (qb.grad, kb.grad, vb.grad)):
         assert ((a.float() - b.float()).norm() / b.float().norm()).item() < 1e-3
+
+
+def test_fake_dual_forward_backward_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import wan_flash.torch_op as op
+
+    with FakeTensorMode():
+        q, k0, v0 = _fake_inputs(sq=300, skv=512)
+        _, k1, v1 = _fake_inputs(sq=300, skv=257)
+        o0, lse0, o1, lse1 = torch.ops.wan_flash.attn_fwd_dual(q, k0, v0, k1, v1)
+        assert o0.shape == o1.shape == q.shape and o0.dtype == torch.bfloat16
+        assert lse0.shape == lse1.shape == (1, 2, 300) and lse1.dtype == torch.float32
+        g = torch.ops.wan_flash.attn_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, o0, o1)
+        assert [t.shape for t in g] == [q.shape, k0.shape, v0.shape, k1.shape, v1.shape]
+    leaves = [torch.empty(1, s, 2, 128, dtype=torch.bfloat16, device="meta", requires_grad=True)
+              for s in (300, 512, 512, 257, 257)]
+    out = op.wan_attention_dual(*leaves)
+    out.backward(torch.empty_like(out))
+    assert out.shape == leaves[0].shape
+    assert [t.grad.shape for t in leaves] == [t.shape for t in leaves]
+
+
+@pytest.mark.gpu
+def test_dual_ops_match_interface():
+    import wan_flash.torch_op as op
+    from tests.gpu_util import seeded
+    from wan_flash.interface import wan_flash_attn_dual, wan_flash_fwd_dual
+
+    q, k0, v0, do = (t.cuda() for t in seeded(1, 700, 300, 2, seed=29))
+    _, k1, v1, _ = (t.cuda() for t in seeded(1, 700, 130, 2, seed=31))
+    outs = torch.ops.wan_flash.attn_fwd_dual(q, k0, v0, k1, v1)
+    for a, b in zip(outs, wan_flash_fwd_dual(q, k0, v0, k1, v1)):
+        assert torch.equal(a, b)
+    torch.library.opcheck(torch.ops.wan_flash.attn_fwd_dual.default, (q, k0, v0, k1, v1),
+                          test_utils=("test_schema", "test_faketensor"))
+    la = [t.clone().requires_grad_(True) for t in (q, k0, v0, k1, v1)]
+    lb = [t.clone().requires_grad_(True) for t in (q, k0, v0, k1, v1)]
+    oa = op.wan_attention_dual(*la)
+    ob = wan_flash_attn_dual(*lb)
+    assert torch.equal(oa, ob)
+    oa.backward(do)
+    ob.backward(do)
+    for x, y in zip(la, lb):
+        assert ((x.grad.float() - y.grad.float()).norm() / y.grad.float().norm()).item() < 1e-3

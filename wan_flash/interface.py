@@ -158,11 +158,14 @@ def _bwd_impl(q, k, v, o, lse, do, marks=None):
 
 
 def _bwd_multi(q, contexts, do, marks=None):
-    """Backward of sum_c attention(q, k_c, v_c) for one or two KV contexts
-    given o_c, lse_c of each and dO of the sum: the contexts' main kernels
-    add into one dQ accumulator (zeroed by the first preprocess), converted
-    once.  Returns (dq, ((dk_c, dv_c), ...))."""
-    assert do.dtype == torch.bfloat16 and q.dtype == torch.bfloat16 and do.shape == q.shape
+    """Backward of attention(q, k_c, v_c) for one or two KV contexts given
+    o_c, lse_c of each and dO (one tensor: the gradient of the sum of the
+    outputs, or one per context): the contexts' main kernels add into one
+    dQ accumulator (zeroed by the first preprocess), converted once.
+    Returns (dq, ((dk_c, dv_c), ...))."""
+    dos = list(do) if isinstance(do, (list, tuple)) else [do] * len(contexts)
+    assert len(dos) == len(contexts)
+    assert q.dtype == torch.bfloat16 and all(x.dtype == torch.bfloat16 and x.shape == q.shape for x in dos)
     b, sq, h, d = q.shape
     assert d == 128, "specialized for head_dim=128"
     for k, v, o, lse in contexts:
@@ -172,9 +175,10 @@ def _bwd_multi(q, contexts, do, marks=None):
         assert (b, h, d) == (bk, hk, dk_) and v.shape == k.shape
         assert o.shape == q.shape
         assert lse.shape == (b, h, sq)
-        assert all(t.is_cuda and t.device == q.device for t in (k, v, o, lse, do)), \
+        assert all(t.is_cuda and t.device == q.device for t in (k, v, o, lse, *dos)), \
             "tensors must be on one CUDA device"
-    q, do = _aligned(q), _aligned(do)
+    q = _aligned(q)
+    dos = [_aligned(x) for x in dos]
     dq = torch.empty_like(q)
     grads = [(torch.empty_like(k), torch.empty_like(v)) for k, v, _, _ in contexts]
     live = [c for c, (k, _, _, _) in enumerate(contexts) if b > 0 and h > 0 and k.shape[1] > 0]
@@ -197,6 +201,7 @@ def _bwd_multi(q, contexts, do, marks=None):
         for i, c in enumerate(live):
             k, v, o, lse = contexts[c]
             k, v, o = (_aligned(t) for t in (k, v, o))
+            do = dos[c]
             lse = lse if lse.is_contiguous() else lse.contiguous()
             skv = k.shape[1]
             plan = bwd_plan(b, sq, skv, h, _sms(dev))
@@ -216,9 +221,9 @@ def _bwd_multi(q, contexts, do, marks=None):
                 cfg.deterministic, cfg.sem = 1, sem.data_ptr()
             _lib.check(L.wf_bwd_pre(_ptr(o), _ptr(do), _ptr(lse), _ptr(dpsum), _ptr(neg_lse_log2),
                                     _ptr(dq_accum) if i == 0 else None, b, sq, sq_rounded, h, stream))
-            runs.append((k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, sem))
+            runs.append((k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, sem, do))
         _mark(marks, "bwd_main")
-        for k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, _sem in runs:
+        for k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, _sem, do in runs:
             main_dk = dk_accum if dk_accum is not None else dk
             main_dv = dv_accum if dv_accum is not None else dv
             _lib.check(L.wf_bwd_main(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(neg_lse_log2), _ptr(dpsum),
@@ -226,7 +231,7 @@ def _bwd_multi(q, contexts, do, marks=None):
                                      ctypes.byref(cfg), stream))
         _mark(marks, "bwd_convert")
         _lib.check(L.wf_bwd_convert(_ptr(dq_accum), _ptr(dq), ctypes.c_float(1.0 / math.sqrt(d)), b, sq, h, stream))
-        for k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, _sem in runs:
+        for k, v, skv, dpsum, neg_lse_log2, dk, dv, dk_accum, dv_accum, cfg, _sem, _do in runs:
             if dk_accum is not None:
                 _lib.check(L.wf_bwd_convert(_ptr(dk_accum), _ptr(dk), ctypes.c_float(1.0), b, skv, h, stream))
                 _lib.check(L.wf_bwd_convert(_ptr(dv_accum), _ptr(dv), ctypes.c_float(1.0), b, skv, h, stream))
@@ -265,11 +270,12 @@ def wan_flash_fwd_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: 
     return o0, lse0, o1, lse1
 
 
-def wan_flash_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do):
-    """Backward of o0 + o1 (wan_flash_fwd_dual's outputs) given dO of the
-    sum: (dq, dk0, dv0, dk1, dv1).  Both contexts add into one dQ accumulator
-    that is zeroed and converted once."""
-    dq, ((dk0, dv0), (dk1, dv1)) = _bwd_multi(q, ((k0, v0, o0, lse0), (k1, v1, o1, lse1)), do)
+def wan_flash_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do, do1=None):
+    """Backward of wan_flash_fwd_dual: (dq, dk0, dv0, dk1, dv1) given dO of
+    o0 + o1 (``do``), or of o0 and o1 separately (``do``, ``do1``).  Both
+    contexts add into one dQ accumulator that is zeroed and converted once."""
+    dos = do if do1 is None else (do, do1)
+    dq, ((dk0, dv0), (dk1, dv1)) = _bwd_multi(q, ((k0, v0, o0, lse0), (k1, v1, o1, lse1)), dos)
     return dq, dk0, dv0, dk1, dv1
 
 

@@ -16,14 +16,21 @@ implementations are ``wan_flash_fwd`` / ``wan_flash_bwd`` (the sm_100a
 kernels); nothing here computes on the CPU.
 
 ``wan_attention(q, k, v) -> o`` is the op-based counterpart of
-``wan_flash_attn``.
+``wan_flash_attn``.  The two-context path (Wan I2V text + image cross
+attention) has the same treatment:
+
+    wan_flash::attn_fwd_dual(q, k0, v0, k1, v1) -> (o0, lse0, o1, lse1)
+    wan_flash::attn_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do0, do1)
+        -> (dq, dk0, dv0, dk1, dv1)
+
+and ``wan_attention_dual(q, k0, v0, k1, v1) -> o0 + o1``.
 """
 
 from __future__ import annotations
 
 import torch
 
-from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+from wan_flash.interface import wan_flash_bwd, wan_flash_bwd_dual, wan_flash_fwd, wan_flash_fwd_dual
 
 
 @torch.library.custom_op("wan_flash::attn_fwd", mutates_args=())
@@ -71,3 +78,53 @@ attn_fwd.register_autograd(_backward, setup_context=_setup_context)
 def wan_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """o = softmax(q k^T / sqrt(128)) v through the registered operator (differentiable)."""
     return attn_fwd(q, k, v)[0]
+
+
+@torch.library.custom_op("wan_flash::attn_fwd_dual", mutates_args=())
+def attn_fwd_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: torch.Tensor,
+                  v1: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    o0, lse0, o1, lse1 = wan_flash_fwd_dual(q, k0, v0, k1, v1)
+    return o0, lse0, o1, lse1
+
+
+@attn_fwd_dual.register_fake
+def _attn_fwd_dual_fake(q, k0, v0, k1, v1):
+    b, sq, h, d = q.shape
+    torch._check(d == 128, lambda: "specialized for head_dim=128")
+    lse = q.new_empty((b, h, sq), dtype=torch.float32)
+    return torch.empty_like(q), lse, torch.empty_like(q), torch.empty_like(lse)
+
+
+@torch.library.custom_op("wan_flash::attn_bwd_dual", mutates_args=())
+def attn_bwd_dual(
+    q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: torch.Tensor, v1: torch.Tensor, o0: torch.Tensor,
+    lse0: torch.Tensor, o1: torch.Tensor, lse1: torch.Tensor, do0: torch.Tensor, do1: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    return wan_flash_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do0, do1)
+
+
+@attn_bwd_dual.register_fake
+def _attn_bwd_dual_fake(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do0, do1):
+    return (torch.empty_like(q), torch.empty_like(k0), torch.empty_like(v0), torch.empty_like(k1),
+            torch.empty_like(v1))
+
+
+def _setup_context_dual(ctx, inputs, output):
+    o0, lse0, o1, lse1 = output
+    ctx.save_for_backward(*inputs, o0, lse0, o1, lse1)
+
+
+def _backward_dual(ctx, do0, dlse0, do1, dlse1):
+    # the LSE outputs are not differentiated
+    q, k0, v0, k1, v1, o0, lse0, o1, lse1 = ctx.saved_tensors
+    return attn_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do0.contiguous(), do1.contiguous())
+
+
+attn_fwd_dual.register_autograd(_backward_dual, setup_context=_setup_context_dual)
+
+
+def wan_attention_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: torch.Tensor,
+                       v1: torch.Tensor) -> torch.Tensor:
+    """attention(q, k0, v0) + attention(q, k1, v1) through the registered operators (differentiable)."""
+    o0, _, o1, _ = attn_fwd_dual(q, k0, v0, k1, v1)
+    return o0 + o1
