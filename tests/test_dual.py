@@ -115,3 +115,23 @@ def test_attn_dual_autograd():
     assert rel(out, ref.detach()) <= REL_L2_TOL
     for x, y in zip(leaves, ref_leaves):
         assert rel(x.grad, y.grad) <= REL_L2_TOL
+
+
+def test_bwd_dual_deterministic_bitwise():
+    """deterministic=True: the shared-accumulator backward is bitwise
+    reproducible (each context's main kernel adds in KV-block order; the
+    contexts run one after the other)."""
+    from wan_flash import _lib, features
+    from wan_flash.interface import wan_flash_bwd_dual, wan_flash_fwd_dual
+
+    q, k0, v0, k1, v1, do = _inputs(1, 2, 1500, 512, 257, seed=59)
+    o0, lse0, o1, lse1 = wan_flash_fwd_dual(q, k0, v0, k1, v1)
+    features.set_bwd_overrides(deterministic=True, nsplit=3)
+    try:
+        runs = [wan_flash_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do) for _ in range(3)]
+        _lib.check_device()
+    finally:
+        features.reset()
+    for g in runs[1:]:
+        for a, b in zip(runs[0], g):
+            assert torch.equal(a, b)
