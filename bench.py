@@ -570,6 +570,29 @@ def main():
         if dual:  # one forward; a second preprocess and main; its own split-M converts
             plan1 = interface.bwd_plan(b, sq, DUAL_IMAGE_CONTEXT, h, sms)
             launches_per_step += 2 + (2 if plan1["nsplit"] > 1 else 0)
+        # HBM-side figures: algorithmic bytes per step over the measured time
+        # of the memory-bound kernels, and of the forward (for the short-KV
+        # cross attention, whose intensity sits near the HBM ridge)
+        sq_r = -(-sq // 128) * 128
+        ctx_lens = [skv] + ([DUAL_IMAGE_CONTEXT] if dual else [])
+        act = 2 * b * h * 128  # bytes per row of a bf16 (b, s, h, 128) tensor
+        pre_bytes = sum(2 * sq * act + 4 * b * h * sq + 8 * b * h * sq_r for _ in ctx_lens) + 4 * b * h * sq_r * 128
+        conv_bytes = 4 * b * h * sq_r * 128 + sq * act
+        for n, pl in zip(ctx_lens, [plan] + ([plan1] if dual else [])):
+            if pl["nsplit"] > 1:  # dk and dv accumulators
+                conv_bytes += 2 * (4 * b * h * (-(-n // 128) * 128) * 128 + n * act)
+        fwd_bytes = sq * act * (1 + len(ctx_lens)) + sum(2 * n * act for n in ctx_lens) + 4 * b * h * sq * len(ctx_lens)
+
+        def gbs(nbytes, name):
+            t = kern_ms.get(name)
+            if not t:
+                return None
+            v = nbytes / (t * 1e-3) / 1e9
+            return {"bytes_per_step": nbytes, "gbs": v, "frac_of_hbm": v / peaks["hbm_gbs"]}
+
+        hbm = {"bwd_pre": gbs(pre_bytes, "bwd_pre"), "bwd_convert": gbs(conv_bytes, "bwd_convert"),
+               "fwd": gbs(fwd_bytes, "fwd"), "hbm_peak_gbs": peaks["hbm_gbs"],
+               "note": "algorithmic bytes (each tensor read or written once) over CUDA-event time"}
         cpu = None
         if not args.no_cpu and world == 1:
             cpu = cpu_sample(args.config)
@@ -608,6 +631,7 @@ def main():
                 "peak_source": f"{peaks['source']} burst bf16 (MEASURED_PEAKS.json)" if peaks["source"] == "measured"
                 else "fallback 1.59 PFLOP/s",
             },
+            "hbm": hbm,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clk,
