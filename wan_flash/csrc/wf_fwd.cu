@@ -10,6 +10,8 @@
 // Blackwell design of its own:
 //
 //   work item = 2 query tiles of 128 rows (256 rows) of one (batch, head).
+//   A work item walks one KV context, or two (the I2V text and image
+//   contexts of the same query rows, kMode 2) as consecutive segments.
 //   A CTA runs items blockIdx.x, blockIdx.x + gridDim.x, ...: one item per
 //   CTA (grid = all items), or persistent (grid = SM count) for short KV
 //   sequences, where the per-item prologue and epilogue would otherwise
@@ -17,7 +19,8 @@
 //   item's last blocks and its first QK^T the current item's last PV.
 //   warps 0-3  softmax for query tile 0  (thread = one query row)
 //   warps 4-7  softmax for query tile 1
-//   warp  8    tcgen05.mma issuer (one thread) + TMEM owner
+//   warp  8    tcgen05.mma issuer (converged warp, one elected lane per
+//              instruction) + TMEM owner
 //   warp  9    TMA producer (one thread)
 //   warp  10   O store: one thread sends each staged O tile out with TMA
 //   warp  11   idle (completes warpgroup 2 so it can give registers back)
