@@ -420,14 +420,32 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask)
 }
 
 // Elected-lane forms for a converged MMA warp (every lane must reach the call).
+// Converged-warp issue: elect.sync picks one lane and predicates the
+// instruction in the same asm block (no divergent branch to reconverge).
 __device__ __forceinline__ void mma_ss_e(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-  if (elect_one()) mma_ss(d, a, b, id, acc);
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
 }
 __device__ __forceinline__ void mma_ts_e(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
-  if (elect_one()) mma_ts(d, a, b, id, acc);
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
 }
 __device__ __forceinline__ void mma_commit_e(uint32_t bar) {
-  if (elect_one()) mma_commit(bar);
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
 }
 __device__ __forceinline__ void mma_ss_pair_e(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
   if (elect_one()) mma_ss_pair(d, a, b, id, acc);
