@@ -131,13 +131,13 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   const int m_begin = split * p.m_chunk;
   const int m_end = min(m_begin + p.m_chunk, p.m_blocks);
   const int cnt = m_end - m_begin;
-  // Query-block order, rotated per KV tile: CTAs that run at the same time
-  // then load different Q/dO tiles and reduce into different dQ tiles,
-  // instead of every resident CTA of a head hitting the same L2 lines.
-  // (deterministic mode keeps the natural order: KV block nb then meets each
-  // query block right after KV block nb-1, which it must wait for)
-  const int rot = (cnt > 0 && !p.deterministic) ? nb % cnt : 0;
-  auto qblock = [&](int u) -> int { int j = u + rot; return m_begin + (j >= cnt ? j - cnt : j); };
+  // Query blocks in natural order: the CTAs of a head resident at the same
+  // time walk the same Q/dO tiles together, so each tile is fetched from
+  // HBM about once and served to the others from L2.  (A walk rotated by the
+  // KV block index, which spreads the dQ reductions over more lines,
+  // measured 1-2 % slower.)  Deterministic mode relies on this order: KV
+  // block nb meets each query block just after KV block nb-1.
+  auto qblock = [&](int u) -> int { return m_begin + u; };
   if (cnt <= 0) return;  // empty split: nothing to add (uniform for the CTA)
   const size_t bh = (size_t)b * p.h + h;
 
