@@ -70,7 +70,7 @@ METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/
 # DRAM bytes (read + write) per launch per head, from one ncu capture of the
 # C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd_c2_h4.md);
 # traffic grows with the number of heads, so it is scaled by the run's heads.
-DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 321.86e6 / 4, ("c2", "fwd"): 118.96e6 / 4}
+DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 318.49e6 / 4, ("c2", "fwd"): 118.96e6 / 4}
 NOMINAL_BF16_TFLOPS = 2250.0
 
 
