@@ -330,6 +330,72 @@ def run_c5(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- features A/B
+def run_features_ab(args):
+    """Re-evaluate the features.py flags on B200: each setting against the
+    defaults on the config's shape (1 GPU), forward or backward chain timed
+    with CUDA events on the stream, settings interleaved round-robin over
+    `--steps` rounds (median reported) so clock drift hits all alike."""
+    import torch
+
+    from wan_flash import features, interface
+
+    kind, b, sq, skv, h, seed, desc = CONFIGS[args.config]
+    assert kind in ("self", "cross"), "--features-ab runs on c2, c3 or c3i2v"
+    if args.heads > 0:
+        h = args.heads
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed * 1000)
+
+    def rnd(s):
+        return torch.randn(b, s, h, 128, device=dev, dtype=torch.float32, generator=gen).to(torch.bfloat16)
+
+    q, k, v, do = rnd(sq), rnd(skv), rnd(skv), rnd(sq)
+    f_fwd, f_bwd = flops(b, h, sq, skv)
+    o, lse = interface.wan_flash_fwd(q, k, v)
+    settings = [
+        ("fwd", "defaults", {}, {}),
+        ("fwd", "rescale_skip_threshold=0", {"rescale_skip_threshold": 0.0}, {}),
+        ("fwd", "scheduler=single", {"scheduler": "single"}, {}),
+        ("fwd", "scheduler=persistent", {"scheduler": "persistent"}, {}),
+        ("bwd", "defaults", {}, {}),
+        ("bwd", "cluster_n=2", {}, {"cluster_n": 2}),
+        ("bwd", "deterministic", {}, {"deterministic": True}),
+    ]
+    auto_nsplit = interface.bwd_plan(b, sq, skv, h)["nsplit"]
+    for n in sorted({1, 2, max(1, auto_nsplit // 2), auto_nsplit * 2} - {auto_nsplit}):
+        settings.append(("bwd", f"nsplit={n}", {}, {"nsplit": n}))
+    times = {i: [] for i in range(len(settings))}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for rnd_i in range(args.warmup + args.steps):
+        for i, (what, _, fo, bo) in enumerate(settings):
+            features.reset()
+            features.set_overrides(**fo)
+            features.set_bwd_overrides(**bo)
+            ev0.record()
+            if what == "fwd":
+                interface.wan_flash_fwd(q, k, v)
+            else:
+                interface.wan_flash_bwd(q, k, v, o, lse, do)
+            ev1.record()
+            torch.cuda.synchronize()
+            if rnd_i >= args.warmup:
+                times[i].append(ev0.elapsed_time(ev1))
+    features.reset()
+    base = {}
+    for i, (what, name, fo, bo) in enumerate(settings):
+        ms = statistics.median(times[i])
+        tf = (f_fwd if what == "fwd" else f_bwd) / (ms * 1e-3) / 1e12
+        if name == "defaults":
+            base[what] = tf
+        line = {"features_ab": what, "setting": name, "ms": ms, "tflops": tf,
+                "vs_defaults": tf / base[what] if what in base else None,
+                "config": {"workload": desc, "heads": h}, "rounds": args.steps}
+        print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -341,6 +407,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override heads per GPU (small profiling cases)")
+    ap.add_argument("--features-ab", action="store_true",
+                    help="A/B the features.py flags on --config (c2 or c3): one JSON line per setting")
     ap.add_argument("--bwd-cluster-n", type=int, default=0, choices=[0, 1, 2],
                     help="backward kernel form: 1 = single CTAs, 2 = CTA pairs, 0 = the feature default")
     args = ap.parse_args()
@@ -387,6 +455,8 @@ def main():
 
     if args.config == "c5":
         return run_c5(args, rank, world, local_rank)
+    if args.features_ab:
+        return run_features_ab(args)
 
     if args.bwd_cluster_n:
         features.set_bwd_overrides(cluster_n=args.bwd_cluster_n)
