@@ -27,7 +27,9 @@ Forward flags
 
 Backward flags
   tile_m / tile_n         fixed at 128 x 128.
-  num_stages              Q/dO double buffering (fixed at 2).
+  num_stages              2 (fixed): Q double-buffered; dO single-buffered,
+                          refilled between dV(u) and dP(u+1) (shared
+                          memory holds no second dO tile).
   nsplit                  split-M factor; 0 = auto (1 when the
                           (n_blocks*h*b) grid fills the GPU, otherwise the
                           smallest split with >= 95% wave efficiency).  With
@@ -99,7 +101,7 @@ def _validate_bwd(f: BwdFeatures):
     if f.tile_m != 128 or f.tile_n != 128:
         raise ValueError("the sm_100a backward is built for 128x128 tiles")
     if f.num_stages != 2:
-        raise ValueError("the backward double-buffers Q/dO (num_stages=2)")
+        raise ValueError("the backward's Q/dO staging is fixed (num_stages=2)")
     if f.nsplit < 0:
         raise ValueError("nsplit must be >= 0 (0 = auto)")
     if f.cluster_n not in (1, 2):
