@@ -108,3 +108,84 @@ def test_dual_ops_match_interface():
     ob.backward(do)
     for x, y in zip(la, lb):
         assert ((x.grad.float() - y.grad.float()).norm() / y.grad.float().norm()).item() < 1e-3
+
+
+@pytest.mark.gpu
+def test_op_under_activation_checkpointing():
+    """The op inside torch.utils.checkpoint (full recompute) and under a
+    selective-checkpoint policy that saves the attention outputs (the
+    forward is then not re-run in the backward): gradients match the plain
+    run up to the fp32 reduction order."""
+    from torch.utils.checkpoint import CheckpointPolicy, checkpoint, create_selective_checkpoint_contexts
+
+    import wan_flash.torch_op as op
+    from tests.gpu_util import seeded
+
+    q, k, v, do = (t.cuda() for t in seeded(1, 640, 384, 2, seed=37))
+    w = torch.randn(128, 128, device="cuda", dtype=torch.bfloat16) * 0.05
+
+    def block(q, k, v):
+        return op.wan_attention(q @ w, k, v) @ w
+
+    def policy(ctx, fn, *args, **kwargs):
+        if fn == torch.ops.wan_flash.attn_fwd.default:
+            return CheckpointPolicy.MUST_SAVE
+        return CheckpointPolicy.PREFER_RECOMPUTE
+
+    # count the forward kernel launches through the op's implementation
+    launches = {"n": 0}
+    real_fwd = op.wan_flash_fwd
+
+    def counting_fwd(*a):
+        launches["n"] += 1
+        return real_fwd(*a)
+
+    results, counts = [], []
+    op.wan_flash_fwd = counting_fwd
+    try:
+        for mode in ("plain", "checkpoint", "selective"):
+            launches["n"] = 0
+            leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+            if mode == "plain":
+                out = block(*leaves)
+            elif mode == "checkpoint":
+                out = checkpoint(block, *leaves, use_reentrant=False)
+            else:
+                out = checkpoint(block, *leaves, use_reentrant=False,
+                                 context_fn=lambda: create_selective_checkpoint_contexts(policy))
+            out.backward(do)
+            results.append((out.detach(), [t.grad for t in leaves]))
+            counts.append(launches["n"])
+    finally:
+        op.wan_flash_fwd = real_fwd
+    # full checkpointing re-runs the attention forward in the backward; the
+    # selective policy keeps its outputs, so it runs once
+    assert counts == [1, 2, 1], counts
+    base_out, base_grads = results[0]
+    for out, grads in results[1:]:
+        assert torch.equal(out, base_out)
+        for g, g0 in zip(grads, base_grads):
+            assert ((g.float() - g0.float()).norm() / g0.float().norm()).item() < 1e-3
+
+
+@pytest.mark.gpu
+def test_op_under_torch_compile():
+    """torch.compile traces the op through its fake implementation and runs
+    the kernels; forward and gradients match the eager op."""
+    import wan_flash.torch_op as op
+    from tests.gpu_util import seeded
+
+    q, k, v, do = (t.cuda() for t in seeded(1, 512, 300, 2, seed=41))
+
+    def fn(q, k, v):
+        return op.wan_attention(q, k, v) * 2.0
+
+    compiled = torch.compile(fn, backend="aot_eager", fullgraph=True)
+    la = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    lb = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    oa, ob = fn(*la), compiled(*lb)
+    assert torch.equal(oa, ob)
+    oa.backward(do)
+    ob.backward(do)
+    for x, y in zip(la, lb):
+        assert ((x.grad.float() - y.grad.float()).norm() / x.grad.float().norm()).item() < 1e-3
