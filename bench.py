@@ -4,19 +4,25 @@
                     [--impl ours|reference]
 
 One step = wan_flash_fwd + wan_flash_bwd over one batch of synthetic bf16
-inputs of the configured Wan shape (default C2: Wan2.1-1.3B 480p
-self-attention, b=1, s=32760, h=12, d=128, q/k/v/dO ~ N(0,1), seed 1).
+inputs of the configured Wan shape (default C4: Wan2.1-14B 720p
+self-attention, b=1, s=75600, 40 heads, d=128, q/k/v/dO ~ N(0,1), seed 3,
+head-sharded over the GPUs: 40/N heads per rank).
 TFLOP/s counts 4*b*h*sq*skv*128 for the forward and 2.5x that for the
 backward (the reference's convention, bench/bench.py:89-93).
 
 Multi-GPU (torchrun, one rank per GPU): the work shards by heads with no
-data-path collective.  C2 runs as weak scaling (every rank owns 12 heads of a
-12*N-head problem); C4 (Wan2.1-14B 720p, 40 heads) runs as strong scaling
-(40/N heads per rank).  C5 is the sequence-parallel Wan block: activations
-sequence-sharded (1, 75600/N, 40, 128) per rank, Ulysses all-to-all to head
-shards, self- and cross-attention forward + backward, all-to-all back; it
-reports the exposed communication (step time minus the same attention
-work without the exchanges).  Time is the max over ranks of CUDA-event time.
+data-path collective.  C4 (Wan2.1-14B 720p, 40 heads) runs as strong scaling
+(40/N heads per rank); C2 and the cross-attention configs run as weak
+scaling (every rank owns the config's heads of an N-times-larger problem).
+C5 is the sequence-parallel Wan block: activations sequence-sharded
+(1, 75600/N, 40, 128) per rank, Ulysses all-to-all to head shards, self- and
+cross-attention forward + backward, all-to-all back; it reports the exposed
+communication (step time minus the same attention work without the
+exchanges) and checks its outputs and query gradient against attention
+computed without the all-to-all (full K/V gathered along the sequence).  At
+N > 1 the default C4 run also runs the C5 block in the same invocation and
+adds it to the line as ``sp_block``.  Time is the max over ranks of
+CUDA-event time.
 
 Printed (rank 0): one JSON line with value (whole-job TFLOP/s, inputs
 resident in HBM), e2e (same metric through the public API with every step's
@@ -72,6 +78,33 @@ METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/
 # traffic grows with the number of heads, so it is scaled by the run's heads.
 DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 318.49e6 / 4, ("c2", "fwd"): 118.96e6 / 4}
 NOMINAL_BF16_TFLOPS = 2250.0
+
+
+STRONG_SCALING = {"c4", "c5"}  # total work fixed as N grows (heads split over the ranks)
+
+
+def heads_layout(cfg_name: str, world: int, heads_override: int = 0):
+    """(heads per rank, heads of the whole job, scaling) of a config at N ranks."""
+    h_total = CONFIGS[cfg_name][4]
+    if heads_override > 0:
+        return heads_override, heads_override * world, "weak"
+    if cfg_name in STRONG_SCALING:
+        assert h_total % world == 0, f"{h_total} heads must split evenly over {world} ranks"
+        return h_total // world, h_total, "strong"
+    return h_total, h_total * world, "weak"
+
+
+def config_dict(cfg_name: str, world: int, heads_override: int = 0) -> dict:
+    """The line's ``config`` object; both arms (ours and --impl reference)
+    print the same one for the same workload."""
+    kind, b, sq, skv, _, _, desc = CONFIGS[cfg_name]
+    h, global_h, _ = heads_layout(cfg_name, world, heads_override)
+    return {
+        "workload": desc, "global_batch": b, "seq_len": sq,
+        "kv_len": [skv, DUAL_IMAGE_CONTEXT] if kind == "dual" else skv, "heads_per_gpu": h,
+        "heads_total": global_h, "head_dim": 128, "parallelism": f"heads/{world}",
+        "l2": "inputs larger than L2 (q/k/v/dO/o/grad working set >> 126 MB); no flush",
+    }
 
 
 def load_peaks():
@@ -150,6 +183,20 @@ def _cpu_threads() -> int:
         return 1
 
 
+def _use_all_cores() -> int:
+    """Give numpy's BLAS every host core (torchrun sets OMP_NUM_THREADS=1 for
+    its ranks, which would otherwise leave the CPU arm on one thread) and
+    return the thread count actually in use."""
+    try:
+        import numpy  # noqa: F401  (threadpoolctl only sees BLAS libraries already loaded)
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(os.cpu_count() or 1)
+    except Exception:
+        pass
+    return _cpu_threads()
+
+
 class CpuSampler:
     """The oracle port (fp32 numpy, oracle/oracle.py) on a bounded sample of
     the workload: head 0, ``rows`` query rows against the full K/V, forward +
@@ -205,30 +252,25 @@ def cpu_sample(cfg_name: str, target_s: float = 12.0):
 
 
 # --------------------------------------------------------------------------- C5 (sequence parallel)
-def run_c5(args, rank, world, local_rank):
+def c5_measure(args, rank, world, dev, group):
     """One step = the attention of a sequence-parallel Wan block, forward and
     backward, through wan_flash.ulysses.ulysses_attention_block: q/k/v/dO
     sequence-sharded per rank, a 512-token context replicated, exchanges
     overlapped with the attention work that does not need them.  Exposed
     communication = step time minus the time of the same local attention on
-    head-sharded inputs."""
+    head-sharded inputs.  Returns (a dict of timings and parity, the step's
+    FLOPs for the whole job, the kernel launches per step); the process
+    group, if any, is the caller's."""
     import torch
     import torch.distributed as dist
 
     from wan_flash import _lib
-    from wan_flash.interface import wan_flash_attn
+    from wan_flash.interface import bwd_plan, wan_flash_attn
     from wan_flash.ulysses import shard_heads, ulysses_attention_block
 
     kind, b, S, _, H, seed, desc = CONFIGS["c5"]
     L = C5_CONTEXT
     assert S % world == 0 and H % world == 0, "75600 tokens and 40 heads must split evenly over the ranks"
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    group = dist.group.WORLD if world > 1 else None
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed * 1000 + rank)
 
@@ -247,6 +289,7 @@ def run_c5(args, rank, world, local_rank):
     qh, kh, vh = (rnd(b, S, hp, 128, grad=True) for _ in range(3))
     doh_s, doh_c = rnd(b, S, hp, 128), rnd(b, S, hp, 128)
     ckh, cvh = (shard_heads(t.detach(), rank, world).contiguous().requires_grad_(True) for t in (ck, cv))
+    out = {}
 
     def sp_step():
         for t in (q, k, v, ck, cv):
@@ -256,6 +299,7 @@ def run_c5(args, rank, world, local_rank):
         else:
             o_s, o_c = wan_flash_attn(q, k, v), wan_flash_attn(q, ck, cv)
         torch.autograd.backward((o_s, o_c), (do_self, do_cross))
+        out["o_s"], out["o_c"] = o_s.detach(), o_c.detach()
 
     def local_step():
         for t in (qh, kh, vh, ckh, cvh):
@@ -265,14 +309,14 @@ def run_c5(args, rank, world, local_rank):
 
     def barrier():
         if world > 1:
-            dist.barrier()
+            dist.barrier(group=group)
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
         if world == 1:
             return x
         t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
         return float(t.item())
 
     def timed(fn):
@@ -287,38 +331,103 @@ def run_c5(args, rank, world, local_rank):
         barrier()
         return max_over_ranks(e0.elapsed_time(e1)) / args.steps
 
-    clocks = ClockSampler(local_rank)
-    clocks.start()
     ms = timed(sp_step)
-    clk = clocks.stop()
     local_ms = timed(local_step)
     _lib.check_device()
+    parity = c5_parity(q, k, v, ck, cv, do_self, do_cross, out["o_s"], out["o_c"], group, world)
     f_self, fb_self = flops(b, H, S, S)
     f_cross, fb_cross = flops(b, H, S, L)
     step_flops = f_self + fb_self + f_cross + fb_cross  # whole job (all ranks)
-    if rank == 0:
-        from wan_flash.interface import bwd_plan
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    launches = sum(1 + 3 + (2 if bwd_plan(b, S, skv, hp, sms)["nsplit"] > 1 else 0) for skv in (S, L))
+    # one all-to-all per tensor: q, k, v in; o out (x2 outputs); dO in (x2); dq, dk, dv back
+    a2a_bytes = b * s_loc * H * 128 * 2 * (world - 1) / world
+    res = {
+        "workload": desc, "ms_per_step": ms, "tflops": step_flops / (ms * 1e-3) / 1e12,
+        "attention_only_ms": local_ms,
+        "attention_only_tflops_per_gpu": step_flops / world / (local_ms * 1e-3) / 1e12,
+        "exposed_comm_ms": max(0.0, ms - local_ms),
+        "exposed_comm_frac": max(0.0, ms - local_ms) / ms,
+        "all_to_all_bytes_per_tensor_per_rank": a2a_bytes,
+        "parity": parity,
+    }
+    return res, step_flops, launches
 
-        sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        launches = sum(1 + 3 + (2 if bwd_plan(b, S, skv, hp, sms)["nsplit"] > 1 else 0) for skv in (S, L))
+
+def c5_parity(q, k, v, ck, cv, do_self, do_cross, o_s, o_c, group, world):
+    """Check the sequence-parallel block's outputs and query gradient against
+    attention computed without the all-to-all: K and V are gathered along the
+    sequence (all_gather, not the all-to-all under test) and this rank's
+    query rows attend them directly with all heads.  o_self and o_cross are
+    per-row computations of the same kernels (expected bitwise equal); dq
+    differs only by the fp32 reduction order.  Gate: rel_l2 <= 4.5e-3, the
+    test suite's tolerance.  Worst over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from wan_flash.interface import wan_flash_bwd, wan_flash_fwd
+
+    def gather_seq(t):
+        if world == 1:
+            return t.detach()
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.detach().contiguous(), group=group)
+        return torch.cat(parts, dim=1)
+
+    def rel(x, y):
+        return ((x.float() - y.float()).norm() / y.float().norm().clamp_min(1e-30)).item()
+
+    with torch.no_grad():
+        qd = q.detach()
+        kf, vf = gather_seq(k), gather_seq(v)
+        o_ref, lse_ref = wan_flash_fwd(qd, kf, vf)
+        oc_ref, lsec_ref = wan_flash_fwd(qd, ck.detach(), cv.detach())
+        dq_s, _, _ = wan_flash_bwd(qd, kf, vf, o_ref, lse_ref, do_self)
+        dq_c, _, _ = wan_flash_bwd(qd, ck.detach(), cv.detach(), oc_ref, lsec_ref, do_cross)
+        dq_ref = (dq_s.float() + dq_c.float()).to(torch.bfloat16)
+        errs = [rel(o_s, o_ref), rel(o_c, oc_ref), rel(q.grad, dq_ref),
+                float((o_s.float() - o_ref.float()).abs().max())]
+        del kf, vf
+    t = torch.tensor(errs, device=q.device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    e = t.tolist()
+    return {"o_self_rel_l2": e[0], "o_cross_rel_l2": e[1], "dq_rel_l2": e[2], "o_self_max_abs": e[3],
+            "tolerance_rel_l2": 4.5e-3, "ok": all(x <= 4.5e-3 for x in e[:3]),
+            "against": "attention of this rank's rows over K/V gathered along the sequence, no all-to-all"}
+
+
+def run_c5(args, rank, world, local_rank):
+    """--config c5: the sequence-parallel block as the line's workload."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    res, step_flops, launches = c5_measure(args, rank, world, dev, group)
+    clk = clocks.stop()
+    if rank == 0:
+        kind, b, S, _, H, seed, desc = CONFIGS["c5"]
         peaks = load_peaks()
-        value = step_flops / (ms * 1e-3) / 1e12
-        local_tf = step_flops / world / (local_ms * 1e-3) / 1e12
-        # one all-to-all per tensor: q, k, v in; o out (x2 outputs); dO in (x2); dq, dk, dv back
-        a2a_bytes = b * s_loc * H * 128 * 2 * (world - 1) / world
+        local_tf = res["attention_only_tflops_per_gpu"]
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; no dataset)",
-            "config": {"workload": desc, "global_batch": b, "seq_len": S, "kv_len": S, "context_len": L,
-                       "heads_total": H, "heads_per_gpu": hp, "head_dim": 128,
+            "metric": METRIC, "value": res["tflops"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16; no dataset)",
+            "config": {"workload": desc, "global_batch": b, "seq_len": S, "kv_len": S, "context_len": C5_CONTEXT,
+                       "heads_total": H, "heads_per_gpu": H // world, "head_dim": 128,
                        "parallelism": f"ulysses sp{world}",
                        "l2": "inputs larger than L2 (activations >> 126 MB); no flush"},
-            "attention_only_ms": local_ms,
-            "attention_only_tflops_per_gpu": local_tf,
-            "exposed_comm_ms": max(0.0, ms - local_ms),
-            "exposed_comm_frac": max(0.0, ms - local_ms) / ms,
-            "all_to_all_bytes_per_tensor_per_rank": a2a_bytes,
+            **{k: res[k] for k in ("attention_only_ms", "attention_only_tflops_per_gpu", "exposed_comm_ms",
+                                   "exposed_comm_frac", "all_to_all_bytes_per_tensor_per_rank", "parity")},
             "roofline": {"kernel": "attention (fwd+bwd, local)", "bound": "tensor", "achieved": local_tf,
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": local_tf / peaks["bf16_tflops"],
                          "traffic": None},
@@ -402,10 +511,13 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=0.0,
+                    help="--impl reference: seconds of CPU work per step (0 = sized so the run ends in minutes)")
+    ap.add_argument("--no-sp", action="store_true", help="at N > 1, skip the sequence-parallel block (C5) run")
     ap.add_argument("--heads", type=int, default=0, help="override heads per GPU (small profiling cases)")
     ap.add_argument("--features-ab", action="store_true",
                     help="A/B the features.py flags on --config (c2 or c3): one JSON line per setting")
@@ -422,26 +534,26 @@ def main():
     if args.impl == "reference":
         # rank 0 alone runs the CPU reference arm; other ranks exit without work
         if rank == 0:
+            world = world if world > 1 else max(1, args.gpus)  # the arm it stands beside
+            cores = _use_all_cores()
             sampler = CpuSampler(args.config)
-            per_step_s = min(20.0, max(1.0, 150.0 / (args.steps + args.warmup)))
+            per_step_s = args.cpu_seconds or min(20.0, max(1.0, 150.0 / (args.steps + args.warmup)))
             rows = sampler.rows_for(per_step_s)
             for _ in range(args.warmup):
                 sampler.run(rows)
             t = sum(sampler.run(rows) for _ in range(args.steps))
             value = sampler.flops(rows) * args.steps / t / 1e12
-            cpu = {"value": value, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port",
+            cpu = {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                    "sample": (f"per step: oracle/oracle.py fp32 fwd+bwd on head 0, {rows} of {sq} query rows x "
                               f"{' + '.join(str(kk.shape[2]) for kk, _ in sampler.kv)} keys; cost is linear in rows "
                               f"and heads")}
             line = {
                 "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True,
-                "scaling": "weak" if args.config != "c4" else "strong",
+                "scaling": heads_layout(args.config, world, args.heads)[2],
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded)",
-                "config": {"workload": desc, "global_batch": b, "seq_len": sq,
-                           "kv_len": [skv, DUAL_IMAGE_CONTEXT] if kind == "dual" else skv,
-                           "heads": h_total, "parallelism": "host cores"},
+                "config": config_dict(args.config, world, args.heads),
                 "cpu_baseline": cpu,
                 "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             }
@@ -468,18 +580,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    if args.config == "c4":
-        assert h_total % world == 0, "40 heads must split evenly over the ranks"
-        h = h_total // world
-        scaling = "strong"
-        global_h = h_total
-    else:
-        h = h_total
-        scaling = "weak"
-        global_h = h_total * world
-    if args.heads > 0:
-        h = args.heads
-        global_h = h * world
+    h, global_h, scaling = heads_layout(args.config, world, args.heads)
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed * 1000 + rank)
@@ -623,6 +724,16 @@ def main():
     clk = clocks.stop()
     _lib.check_device()
 
+    # At N > 1 the default (C4, head-sharded) run also measures the
+    # sequence-parallel block (C5: Ulysses all-to-alls around the same
+    # attention) so the collective path is timed and checked in every scaling
+    # run; every rank takes part.
+    sp_block = None
+    if world > 1 and args.config == "c4" and args.heads == 0 and not args.no_sp:
+        sp_res, sp_flops, sp_launches = c5_measure(args, rank, world, dev, dist.group.WORLD)
+        sp_block = {**sp_res, "n_gpus": world, "gpu_launches": sp_launches * args.steps,
+                    "note": "separate timed region after the C4 steps; not part of value or ms_per_step"}
+
     if rank == 0:
         peaks = load_peaks()
         value = step_flops * world / (ms_per_step * 1e-3) / 1e12
@@ -679,12 +790,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16; no dataset)",
-            "config": {
-                "workload": desc, "global_batch": b, "seq_len": sq,
-                "kv_len": [skv, DUAL_IMAGE_CONTEXT] if dual else skv, "heads_per_gpu": h,
-                "heads_total": global_h, "head_dim": 128, "parallelism": f"heads/{world}",
-                "l2": "inputs larger than L2 (q/k/v/dO/o/grad working set >> 126 MB); no flush",
-            },
+            "config": config_dict(args.config, world, args.heads),
             "fwd_tflops": fwd_tf,
             "bwd_tflops": bwd_tf,
             "bwd_main_tflops": main_tf,
@@ -706,6 +812,7 @@ def main():
             "e2e": e2e,
             "clocks": clk,
             "gpu_launches": launches_per_step * args.steps,
+            "sp_block": sp_block,
             "bwd_nsplit": plan["nsplit"],
             "bwd_cluster_n": plan["cluster_n"],
         }

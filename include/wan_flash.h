@@ -135,9 +135,8 @@ int wf_bwd_convert(const float* accum, void* out, float scale, int b, int s, int
 /*
  * Backward without caller workspaces: the whole chain of wf_bwd_pre,
  * wf_bwd_main (nsplit = 1) and wf_bwd_convert, with the three fp32
- * workspaces taken from a 64 MiB array compiled into this library.  No
- * counterpart in the reference (its driver always allocates workspaces with
- * torch, wan_flash/interface.py:137-149); it exists for callers that can pass
+ * workspaces taken from a 64 MiB array compiled into this library.  It has
+ * no counterpart in the reference.  It exists for callers that can pass
  * tensors but cannot allocate device memory at call time -- a plugin host
  * that owns every device allocation, or a latency-critical caller that cannot
  * afford cudaMalloc's implicit synchronisation.  It never allocates.

@@ -8,4 +8,3 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU and the built CUDA library")
-    config.addinivalue_line("markers", "slow: true Wan shapes (set WAN_FLASH_SLOW_TESTS=1)")

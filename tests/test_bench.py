@@ -36,3 +36,34 @@ def test_cpu_sampler_single_and_dual():
     rows = 64
     assert dual.flops(rows) == sum(sum(bench.flops(1, 1, rows, n)) for n in (512, bench.DUAL_IMAGE_CONTEXT))
     assert single.run(rows) > 0.0 and dual.run(rows) > 0.0
+
+
+def test_heads_layout_and_shared_config():
+    """C4 is strong-scaled over the 40 heads (40/20/10/5 per GPU); C2 weak."""
+    bench = _bench()
+    for n, hp in ((1, 40), (2, 20), (4, 10), (8, 5)):
+        assert bench.heads_layout("c4", n) == (hp, 40, "strong")
+        cfg = bench.config_dict("c4", n)
+        assert (cfg["heads_per_gpu"], cfg["heads_total"], cfg["parallelism"]) == (hp, 40, f"heads/{n}")
+    assert bench.heads_layout("c2", 8) == (12, 96, "weak")
+    assert bench.heads_layout("c4", 2, heads_override=3) == (3, 6, "weak")
+
+
+def test_reference_arm_uses_all_cores_and_the_same_config():
+    """The CPU reference arm under torchrun's OMP_NUM_THREADS=1 still runs on
+    every host core, and prints the GPU arm's config object."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, OMP_NUM_THREADS="1")  # what torchrun sets for its ranks
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0", "--cpu-seconds", "0.2"], capture_output=True, text=True, env=env,
+                         timeout=300, cwd=str(ROOT))
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    bench = _bench()
+    assert line["impl"] == "reference" and line["config"] == bench.config_dict("c4", 1)
+    assert line["cpu_baseline"]["cores"] == os.cpu_count()
+    assert line["scaling"] == "strong" and line["value"] > 0

@@ -74,3 +74,22 @@ def test_oracle_lse_is_natural_log_and_softmax_normalised():
     p = np.exp(s - lse[0, 0][:, None])
     assert np.allclose(p.sum(-1), 1.0, atol=1e-5)
     assert np.allclose(o[0, 0], p @ v[0, 0], atol=1e-5)
+
+
+def test_oracle_on_row_and_key_slices():
+    """The oracle called on a slice of query rows returns exactly those rows
+    of O, LSE and dQ, and called on a slice of keys (every query row, the
+    given o / lse) exactly those rows of dK and dV: the 75600-token parity
+    test checks the GPU result on such slices."""
+    q, k, v, do = make_inputs(1, 3000, 3000, 1, seed=3)
+    Q, K, V, DO = (to_bhsd_f32(t) for t in (q, k, v, do))
+    O, LSE = oracle_fwd(Q, K, V)
+    fdq, fdk, fdv = oracle_bwd(Q, K, V, O, LSE, DO)
+    for sl in (slice(0, 512), slice(1536 + 64, 2112), slice(2488, 3000)):
+        ro, rl = oracle_fwd(Q[:, :, sl], K, V)
+        assert np.allclose(ro, O[:, :, sl], rtol=1e-5, atol=1e-6) and np.allclose(rl, LSE[:, :, sl], atol=1e-6)
+        rdq, _, _ = oracle_bwd(Q[:, :, sl], K, V, O[:, :, sl], LSE[:, :, sl], DO[:, :, sl])
+        assert np.allclose(rdq, fdq[:, :, sl], rtol=1e-4, atol=1e-6)
+        _, rdk, rdv = oracle_bwd(Q, K[:, :, sl], V[:, :, sl], O, LSE, DO)
+        assert np.allclose(rdk, fdk[:, :, sl], rtol=1e-4, atol=1e-6)
+        assert np.allclose(rdv, fdv[:, :, sl], rtol=1e-4, atol=1e-6)

@@ -40,6 +40,46 @@ def test_fake_forward_backward_shapes():
     assert qg.grad.dtype == torch.bfloat16
 
 
+def test_fake_outputs_contiguous_for_permuted_inputs():
+    """The kernels write contiguous (b, s, h, 128) outputs whatever the
+    inputs' strides; the fakes must report the same strides, or a traced
+    graph would index the real outputs wrongly."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import wan_flash.torch_op  # noqa: F401  (registers the ops)
+
+    def permuted(t):  # dense (b, s, h, d) view of a (b, h, s, d) tensor
+        return t.transpose(1, 2).contiguous().transpose(1, 2)
+
+    with FakeTensorMode():
+        q, k, v = (permuted(t) for t in _fake_inputs())
+        assert not q.is_contiguous()
+        o, lse = torch.ops.wan_flash.attn_fwd(q, k, v)
+        assert o.is_contiguous() and lse.is_contiguous()
+        for g in torch.ops.wan_flash.attn_bwd(q, k, v, permuted(o), lse, permuted(o)):
+            assert g.is_contiguous()
+        _, k1, v1 = (permuted(t) for t in _fake_inputs(skv=257))
+        outs = torch.ops.wan_flash.attn_fwd_dual(q, k, v, k1, v1)
+        assert all(t.is_contiguous() for t in outs)
+        g = torch.ops.wan_flash.attn_bwd_dual(q, k, v, k1, v1, outs[0], outs[1], outs[2], outs[3], outs[0], outs[2])
+        assert all(t.is_contiguous() for t in g)
+
+
+def test_lse_outputs_not_differentiable():
+    """LSE carries no gradient (the reference's autograd returns o only): the
+    op marks it non-differentiable instead of dropping its gradient silently."""
+    import wan_flash.torch_op  # noqa: F401
+
+    leaves = [torch.empty(1, s, 2, 128, dtype=torch.bfloat16, device="meta", requires_grad=True)
+              for s in (300, 200, 200, 257, 257)]
+    o, lse = torch.ops.wan_flash.attn_fwd(*leaves[:3])
+    assert o.requires_grad and not lse.requires_grad
+    o0, lse0, o1, lse1 = torch.ops.wan_flash.attn_fwd_dual(*leaves)
+    assert o0.requires_grad and o1.requires_grad and not lse0.requires_grad and not lse1.requires_grad
+    with pytest.raises(RuntimeError):
+        lse.sum().backward()
+
+
 @pytest.mark.gpu
 def test_ops_match_interface_and_opcheck():
     import wan_flash.torch_op as op
@@ -185,6 +225,30 @@ def test_op_under_torch_compile():
     lb = [t.clone().requires_grad_(True) for t in (q, k, v)]
     oa, ob = fn(*la), compiled(*lb)
     assert torch.equal(oa, ob)
+    oa.backward(do)
+    ob.backward(do)
+    for x, y in zip(la, lb):
+        assert ((x.grad.float() - y.grad.float()).norm() / x.grad.float().norm()).item() < 1e-3
+
+
+@pytest.mark.gpu
+def test_op_under_torch_compile_permuted_inputs():
+    """torch.compile over the op fed permuted views ((b, h, s, d) leaves
+    transposed to (b, s, h, d)): the fake strides agree with the real
+    contiguous outputs, so compiled and eager results and gradients match."""
+    import wan_flash.torch_op as op
+    from tests.gpu_util import seeded
+
+    q, k, v, do = (t.cuda() for t in seeded(1, 512, 300, 2, seed=43))
+
+    def fn(qh, kh, vh):
+        return op.wan_attention(qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2)) * 2.0
+
+    compiled = torch.compile(fn, backend="aot_eager", fullgraph=True)
+    la = [t.transpose(1, 2).contiguous().requires_grad_(True) for t in (q, k, v)]
+    lb = [t.detach().clone().requires_grad_(True) for t in la]
+    oa, ob = fn(*la), compiled(*lb)
+    assert torch.equal(oa, ob) and oa.stride() == ob.stride()
     oa.backward(do)
     ob.backward(do)
     for x, y in zip(la, lb):

@@ -107,6 +107,18 @@ def _worker(rank, world, port, result_q):
             torch.testing.assert_close(g, gf[:, sl], rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(ckb.grad, ckf3.grad, rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(cvb.grad, cvf3.grad, rtol=1e-4, atol=1e-5)
+
+        # only the self output reaches the loss: the cross output's gradient
+        # arrives as None and is exchanged as zeros of its (b, S/P, H, D) shape
+        qb, kb, vb = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
+        ckb, cvb = ck.clone().requires_grad_(True), cv.clone().requires_grad_(True)
+        o_s, _ = ulysses.ulysses_attention_block(qb, kb, vb, ckb, cvb, fwd=_ref_fwd, bwd=_ref_bwd)
+        o_s.backward(go[:, sl])
+        qf4, kf4, vf4 = (t.clone().requires_grad_(True) for t in (q, k, v))
+        _ref_attn(qf4, kf4, vf4).backward(go)
+        for g, gf in zip((qb.grad, kb.grad, vb.grad), (qf4.grad, kf4.grad, vf4.grad)):
+            torch.testing.assert_close(g, gf[:, sl], rtol=1e-4, atol=1e-5)
+        assert float(ckb.grad.abs().max()) == 0.0 and float(cvb.grad.abs().max()) == 0.0
         result_q.put((rank, "ok"))
     except Exception as e:  # report to the parent
         result_q.put((rank, repr(e)))

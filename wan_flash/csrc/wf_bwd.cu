@@ -91,9 +91,6 @@ static_assert(kSmemUsed <= kSmemLimit, "backward shared memory exceeds the sm_10
 
 size_t bwd_smem_bytes() { return bwd::kSmemBytes; }
 
-// Fraction of exponent pairs evaluated by the FMA-pipe polynomial (0 = none).
-constexpr int kBwdPolyEvery = 0;
-
 enum : uint32_t { kRoleEw = 11, kRoleDq = 12, kRoleBwdMma = 13, kRoleBwdLoad = 14, kRoleEpi = 15 };
 
 __device__ __forceinline__ uint32_t dynamic_smem_size() {
@@ -314,9 +311,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tmem_wait_ld();
       reg_fence32(s[0]);
       reg_fence32(s[1]);
-      // P^T = 2^(S^T * scale_log2 + neg_lse_log2[q]) (MUFU; with kBwdPolyEvery > 0
-      // one pair in kBwdPolyEvery uses the FMA-pipe polynomial).  Rows past the K
-      // tail are zeroed.
+      // P^T = 2^(S^T * scale_log2 + neg_lse_log2[q]) on the MUFU pipe.  Rows past
+      // the K tail are zeroed.
       uint64_t pp[2][16];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -329,7 +325,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
             const int i = 2 * v + e;
             const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2,
                                       e ? f2_pack(L.z, L.w) : f2_pack(L.x, L.y));
-            pp[c][i] = (kBwdPolyEvery > 0 && (i % (kBwdPolyEvery > 0 ? kBwdPolyEvery : 1)) == kBwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
+            pp[c][i] = exp2_mufu2(x);
             float p0, p1;
             f2_unpack(pp[c][i], p0, p1);
             pk[i] = kv_valid ? pack_bf16(p0, p1) : 0u;

@@ -602,37 +602,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair of floats on the FMA/ALU pipes (no MUFU):
-// Cody-Waite reduction x = j + f, j = rint(x) via the 1.5 * 2^23 rounding
-// constant, f in [-1/2, 1/2]; p(f) is the degree-4 polynomial minimising the
-// relative error to 2^f on [-1/2, 1/2] (Remez exchange fit, coefficients from
-// wan_flash/csrc/fit_exp2_poly.py; max relative error 2.7e-6 in fp32, mean
-// 4e-8 -- far below the bf16 rounding of P and the 1e-5 LSE tolerance); the
-// result is p(f) with j added to its exponent field by one integer
-// multiply-add.  Inputs are clamped to >= -126 so the exponent stays normal;
-// -inf gives ~2^-126 (weight zero in bf16 and in the fp32 row sums).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  float x0, x1;
-  f2_unpack(x, x0, x1);
-  x0 = fmaxf(x0, -126.f);
-  x1 = fmaxf(x1, -126.f);
-  const uint64_t xc = f2_pack(x0, x1);
-  const uint64_t t = f2_add(xc, f2_pack(kRound, kRound));
-  const uint64_t j = f2_add(t, f2_pack(-kRound, -kRound));
-  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), xc);
-  uint64_t pl = f2_fma(f2_pack(9.570102207e-03f, 9.570102207e-03f), f, f2_pack(5.591785908e-02f, 5.591785908e-02f));
-  pl = f2_fma(pl, f, f2_pack(2.402474433e-01f, 2.402474433e-01f));
-  pl = f2_fma(pl, f, f2_pack(6.931217909e-01f, 6.931217909e-01f));
-  pl = f2_fma(pl, f, f2_pack(9.999992847e-01f, 9.999992847e-01f));
-  float t0, t1, p0, p1;
-  f2_unpack(t, t0, t1);
-  f2_unpack(pl, p0, p1);
-  // the low bits of t hold j (two's complement); j * 2^23 moves it to the exponent
-  p0 = __int_as_float(__float_as_int(t0) * (1 << 23) + __float_as_int(p0));
-  p1 = __int_as_float(__float_as_int(t1) * (1 << 23) + __float_as_int(p1));
-  return f2_pack(p0, p1);
-}
 // 2^x for a pair on the MUFU pipe.
 __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x) {
   float x0, x1;

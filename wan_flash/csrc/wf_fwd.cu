@@ -81,11 +81,7 @@ enum : uint32_t { kRoleSoftmax0 = 1, kRoleSoftmax1 = 2, kRoleMma = 3, kRoleLoad 
 // TMEM as bf16 pairs over the already-read S columns and the fp32 partial
 // row sum is returned.  Packed f32x2 math keeps the instruction count low:
 // the softmax warps share their SMSPs with the MMA-issuing warp, whose issue
-// rate sets the tensor pipe's.  kFwdPolyEvery > 0 routes one pair in
-// kFwdPolyEvery through the FMA-pipe polynomial exp2 instead of MUFU (off by
-// default: on B200 it costs more issue slots than the MUFU time it saves).
-constexpr int kFwdPolyEvery = 0;
-
+// rate sets the tensor pipe's.
 __device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0, uint32_t tS, uint64_t sl2x2,
                                               uint64_t negx2) {
   uint64_t acc[4];
@@ -98,8 +94,7 @@ __device__ __forceinline__ float fwd_exp_half(const uint32_t (&s)[4][32], int c0
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2, negx2);
-      const uint64_t pp =
-          (kFwdPolyEvery > 0 && (i % (kFwdPolyEvery > 0 ? kFwdPolyEvery : 1)) == kFwdPolyEvery - 1) ? exp2_poly2(x) : exp2_mufu2(x);
+      const uint64_t pp = exp2_mufu2(x);
       acc[i & 3] = f2_add(acc[i & 3], pp);
       float p0, p1;
       f2_unpack(pp, p0, p1);

@@ -179,8 +179,11 @@ def _bwd_multi(q, contexts, do, marks=None):
             "tensors must be on one CUDA device"
     q = _aligned(q)
     dos = [_aligned(x) for x in dos]
-    dq = torch.empty_like(q)
-    grads = [(torch.empty_like(k), torch.empty_like(v)) for k, v, _, _ in contexts]
+    # the kernels write dq/dk/dv as contiguous (b, s, h, 128): allocate them
+    # contiguous whatever the strides of the (possibly permuted) inputs
+    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    grads = [(torch.empty(k.shape, dtype=k.dtype, device=k.device),
+              torch.empty(v.shape, dtype=v.dtype, device=v.device)) for k, v, _, _ in contexts]
     live = [c for c, (k, _, _, _) in enumerate(contexts) if b > 0 and h > 0 and k.shape[1] > 0]
     if sq == 0:
         for dk, dv in grads:

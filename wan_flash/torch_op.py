@@ -39,11 +39,18 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> tuple[torch.T
     return o, lse
 
 
+def _like(t: torch.Tensor) -> torch.Tensor:
+    """A contiguous tensor of t's shape, dtype and device: the real ops write
+    contiguous (b, s, h, 128) outputs whatever the inputs' strides, so the fake
+    outputs must not inherit a permuted input's strides."""
+    return torch.empty(t.shape, dtype=t.dtype, device=t.device)
+
+
 @attn_fwd.register_fake
 def _attn_fwd_fake(q, k, v):
     b, sq, h, d = q.shape
     torch._check(d == 128, lambda: "specialized for head_dim=128")
-    return torch.empty_like(q), q.new_empty((b, h, sq), dtype=torch.float32)
+    return _like(q), q.new_empty((b, h, sq), dtype=torch.float32)
 
 
 @torch.library.custom_op("wan_flash::attn_bwd", mutates_args=())
@@ -56,17 +63,20 @@ def attn_bwd(
 
 @attn_bwd.register_fake
 def _attn_bwd_fake(q, k, v, o, lse, do):
-    return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    return _like(q), _like(k), _like(v)
 
 
 def _setup_context(ctx, inputs, output):
     q, k, v = inputs
     o, lse = output
+    # The LSE output carries no gradient (the reference's autograd function
+    # returns o only): it is marked non-differentiable, so a loss that uses
+    # it gets no gradient through it instead of a silently wrong one.
+    ctx.mark_non_differentiable(lse)
     ctx.save_for_backward(q, k, v, o, lse)
 
 
 def _backward(ctx, do, dlse):
-    # the LSE output is not differentiated (as in the reference, which returns o only)
     q, k, v, o, lse = ctx.saved_tensors
     dq, dk, dv = attn_bwd(q, k, v, o, lse, do.contiguous())
     return dq, dk, dv
@@ -91,8 +101,7 @@ def attn_fwd_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: torch
 def _attn_fwd_dual_fake(q, k0, v0, k1, v1):
     b, sq, h, d = q.shape
     torch._check(d == 128, lambda: "specialized for head_dim=128")
-    lse = q.new_empty((b, h, sq), dtype=torch.float32)
-    return torch.empty_like(q), lse, torch.empty_like(q), torch.empty_like(lse)
+    return _like(q), q.new_empty((b, h, sq), dtype=torch.float32), _like(q), q.new_empty((b, h, sq), dtype=torch.float32)
 
 
 @torch.library.custom_op("wan_flash::attn_bwd_dual", mutates_args=())
@@ -105,17 +114,16 @@ def attn_bwd_dual(
 
 @attn_bwd_dual.register_fake
 def _attn_bwd_dual_fake(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do0, do1):
-    return (torch.empty_like(q), torch.empty_like(k0), torch.empty_like(v0), torch.empty_like(k1),
-            torch.empty_like(v1))
+    return _like(q), _like(k0), _like(v0), _like(k1), _like(v1)
 
 
 def _setup_context_dual(ctx, inputs, output):
     o0, lse0, o1, lse1 = output
+    ctx.mark_non_differentiable(lse0, lse1)  # as in the one-context op
     ctx.save_for_backward(*inputs, o0, lse0, o1, lse1)
 
 
 def _backward_dual(ctx, do0, dlse0, do1, dlse1):
-    # the LSE outputs are not differentiated
     q, k0, v0, k1, v1, o0, lse0, o1, lse1 = ctx.saved_tensors
     return attn_bwd_dual(q, k0, v0, k1, v1, o0, lse0, o1, lse1, do0.contiguous(), do1.contiguous())
 

@@ -218,14 +218,22 @@ class _UlyssesBlock(torch.autograd.Function):
         o_s = _unpack_h2s(ros)
         ctx.save_for_backward(qh, kh, vh, ckh, cvh, o_sh, lse_s, o_ch, lse_c)
         ctx.group, ctx.P, ctx.hp, ctx.bwd = group, P, hp, bwd
+        ctx.out_shape = o_s.shape  # sequence-sharded (b, S/P, H, D), both outputs
+        # an output unused by the loss arrives as None (no zeros materialised
+        # by autograd); backward makes the zeros it exchanges itself
+        ctx.set_materialize_grads(False)
         return o_s, o_c
 
     @staticmethod
     def backward(ctx, g_s, g_c):
         qh, kh, vh, ckh, cvh, o_sh, lse_s, o_ch, lse_c = ctx.saved_tensors
         group, P, bwd = ctx.group, ctx.P, ctx.bwd
-        g_s = torch.zeros_like(o_sh) if g_s is None else g_s
-        g_c = torch.zeros_like(o_ch) if g_c is None else g_c
+        # an output that did not reach the loss has no gradient: zeros of the
+        # sequence-sharded output shape (not the head-sharded o_sh / o_ch)
+        if g_s is None:
+            g_s = torch.zeros(ctx.out_shape, dtype=o_sh.dtype, device=o_sh.device)
+        if g_c is None:
+            g_c = torch.zeros(ctx.out_shape, dtype=o_ch.dtype, device=o_ch.device)
         rgs, wgs = _a2a_start(_pack_s2h(g_s.contiguous(), P), group)
         rgc, wgc = _a2a_start(_pack_s2h(g_c.contiguous(), P), group)
         wgs.wait()
