@@ -76,7 +76,9 @@ METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/
 # DRAM bytes (read + write) per launch per head, from one ncu capture of the
 # C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd_c2_h4.md);
 # traffic grows with the number of heads, so it is scaled by the run's heads.
-DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 318.49e6 / 4, ("c2", "fwd"): 118.96e6 / 4}
+DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 318.49e6 / 4, ("c2", "fwd"): 118.96e6 / 4,
+                       # C4 shape at 4 heads (profiles/dram_c4_h4.md)
+                       ("c4", "bwd_main"): (1223.91e6 + 642.02e6) / 4, ("c4", "fwd"): (263.62e6 + 63.04e6) / 4}
 NOMINAL_BF16_TFLOPS = 2250.0
 
 
@@ -472,6 +474,7 @@ def run_features_ab(args):
         ("bwd", "defaults", {}, {}),
         ("bwd", "cluster_n=2", {}, {"cluster_n": 2}),
         ("bwd", "deterministic", {}, {"deterministic": True}),
+        ("bwd", "pdl=False", {}, {"pdl": False}),
     ]
     auto_nsplit = interface.bwd_plan(b, sq, skv, h)["nsplit"]
     for n in sorted({1, 2, max(1, auto_nsplit // 2), auto_nsplit * 2} - {auto_nsplit}):
@@ -796,6 +799,12 @@ def main():
             "bwd_main_tflops": main_tf,
             "fwd_frac_of_measured_peak": fwd_tf / peaks["bf16_tflops"],
             "bwd_frac_of_measured_peak": bwd_tf / peaks["bf16_tflops"],
+            # the step runs for seconds at the 1 kW power cap, as the driver's
+            # sustained cuBLAS loop does: the fractions of that figure too
+            "frac_of_measured_sustained": ({"fwd": fwd_tf / peaks["bf16_tflops_sustained"],
+                                            "bwd": bwd_tf / peaks["bf16_tflops_sustained"],
+                                            "peak_sustained": peaks["bf16_tflops_sustained"]}
+                                           if peaks.get("bf16_tflops_sustained") else None),
             "frac_of_nominal_2250": {"fwd": fwd_tf / NOMINAL_BF16_TFLOPS, "bwd": bwd_tf / NOMINAL_BF16_TFLOPS},
             "kernel_ms": kern_ms,
             "roofline": {
@@ -803,6 +812,8 @@ def main():
                 "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "traffic": (DRAM_BYTES_PER_HEAD[(args.config, dominant)] * h
                             if (args.config, dominant) in DRAM_BYTES_PER_HEAD else None),
+                "frac_of_sustained": (achieved / peaks["bf16_tflops_sustained"]
+                                      if peaks.get("bf16_tflops_sustained") else None),
                 "traffic_unit": "bytes per launch (ncu capture at 4 heads, scaled by heads)",
                 "peak_source": f"{peaks['source']} burst bf16 (MEASURED_PEAKS.json)" if peaks["source"] == "measured"
                 else "fallback 1.59 PFLOP/s",

@@ -64,7 +64,11 @@ typedef struct wf_bwd_cfg {
   int deterministic; /* 1 = add the fp32 dQ (and split-M dK/dV) contributions in
                         KV-block (split) order: bitwise-reproducible gradients,
                         slower; single-CTA kernel only; needs `sem` */
-  int reserved;
+  int pdl_off;       /* 1 = launch the main kernel without programmatic dependent
+                        launch (default 0: it may start while the preceding
+                        wf_bwd_pre finishes -- barrier set-up, TMEM allocation
+                        and the K/V loads overlap the preprocess's tail -- and
+                        waits for it before reading its outputs) */
   int* sem;          /* deterministic only: b*h*(ceil(sq/128) + ceil(skv/128))
                         int32, zeroed by the caller before each wf_bwd_main */
 } wf_bwd_cfg;
@@ -110,7 +114,9 @@ int wf_bwd_pre(const void* o, const void* dO, const float* lse, float* dpsum, fl
  * Backward main (dK/dV-stationary): dk, dv, and dQ partial sums
  * (fp32 reductions into dq_accum, unscaled).
  * Replaces `compiled[1](*main_args, stream)` of wan_flash/interface.py:191
- * (WanFlashBwdSm90, wan_flash/bwd_sm90.py:381-507).
+ * (WanFlashBwdSm90, wan_flash/bwd_sm90.py:381-507), launched, as there
+ * (use_pdl=True, bwd_sm90.py:498-506), as a programmatic dependent of the
+ * preceding kernel (normally wf_bwd_pre; see wf_bwd_cfg.pdl_off).
  *   nsplit == 1: dk, dv are bf16 (b, skv, h, 128) outputs (dk scaled).
  *   nsplit  > 1: dk, dv are fp32 accumulators of b*h*skv_rounded*128 floats
  *                in the tiled layout of dq_accum (skv_rounded =
@@ -128,7 +134,9 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
  * ((c/4)*64 + r%64)*4 + c%4.
  * Replaces `compiled[2](*post_args, stream)` (dQ) and, under split-M,
  * `compiled[3](...)` (dK, dV) of wan_flash/interface.py:192-195
- * (WanFlashBwdPostprocessSm90, wan_flash/bwd_sm90.py:1140-1308).
+ * (WanFlashBwdPostprocessSm90, wan_flash/bwd_sm90.py:1140-1308).  Launched
+ * as a programmatic dependent of the preceding kernel (the main kernel or the
+ * previous convert), whose completion it waits for before reading `accum`.
  */
 int wf_bwd_convert(const float* accum, void* out, float scale, int b, int s, int h, void* stream);
 

@@ -96,14 +96,14 @@ def test_features_defaults_overrides_and_validation():
 
 
 def test_bwd_cfg_matches_c_struct_and_plan_carries_cluster_n():
-    """wf_bwd_cfg is {int nsplit; int cluster_n; int reserved[2];} in the header."""
+    """wf_bwd_cfg is {int nsplit; int cluster_n; int deterministic; int pdl_off; int* sem;} in the header."""
     import ctypes
 
     from wan_flash import _lib, features
     from wan_flash.interface import bwd_plan
 
     assert ctypes.sizeof(_lib.BwdCfg) == 24
-    assert [f[0] for f in _lib.BwdCfg._fields_] == ["nsplit", "cluster_n", "deterministic", "reserved", "sem"]
+    assert [f[0] for f in _lib.BwdCfg._fields_] == ["nsplit", "cluster_n", "deterministic", "pdl_off", "sem"]
     cfg = _lib.BwdCfg(3, 2)
     assert (cfg.nsplit, cfg.cluster_n, cfg.deterministic, cfg.sem) == (3, 2, 0, None)
     try:

@@ -39,7 +39,7 @@ class FwdCfg(ctypes.Structure):
 
 class BwdCfg(ctypes.Structure):
     _fields_ = [("nsplit", ctypes.c_int), ("cluster_n", ctypes.c_int), ("deterministic", ctypes.c_int),
-                ("reserved", ctypes.c_int), ("sem", ctypes.c_void_p)]
+                ("pdl_off", ctypes.c_int), ("sem", ctypes.c_void_p)]
 
 
 class WanFlashError(RuntimeError):

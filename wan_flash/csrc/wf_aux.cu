@@ -39,6 +39,10 @@ __global__ void __launch_bounds__(256) wf_bwd_pre_kernel(const __nv_bfloat16* __
                                                          float* __restrict__ neg_lse_log2,
                                                          float* __restrict__ dq_accum, int sq, int sq_rounded,
                                                          int h_total) {
+  // the main kernel (launched as a programmatic dependent) may be scheduled
+  // as soon as every CTA of this grid is running; it waits for this grid's
+  // completion before reading what is written here
+  griddep_launch_dependents();
   const int h = blockIdx.y, b = blockIdx.z;
   const size_t bh = (size_t)b * h_total + h;
   const int row0 = blockIdx.x * 64;
@@ -81,6 +85,10 @@ __global__ void __launch_bounds__(256) wf_convert_kernel(const float* __restrict
                                                          __nv_bfloat16* __restrict__ out, float scale, int s_len,
                                                          int s_rounded, int h_total) {
   __shared__ float tile[32][132];
+  // launched as a programmatic dependent of the kernel that filled `accum`
+  // (the backward main kernel, or the previous convert): wait for it
+  griddep_launch_dependents();
+  griddep_wait();
   const int h = blockIdx.y, b = blockIdx.z;
   const size_t bh = (size_t)b * h_total + h;
   const int row0 = blockIdx.x * 32;

@@ -157,6 +157,13 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // Launched as a programmatic dependent of the preprocess: q, k, v, dO were
+  // complete before it started, so barrier set-up, TMEM allocation and the
+  // K/V loads overlap its tail; -lse*log2(e), D and the zeroed dQ
+  // accumulator are touched only after griddep_wait() (the TMA producer,
+  // before the first -lse/D load; the dQ reducing thread, before its first
+  // reduction).  The convert that follows may be scheduled early too.
+  griddep_launch_dependents();
 
   if (warp >= 14) {
     regs_dec<kRegsOther>();  // idle warps of warpgroup 3
@@ -173,6 +180,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         tma_load_4d(sbase + kOffK + x * kBoxBytes, &tm_k, bar(kBarKvFull), x * 64, n0, h, b);
         tma_load_4d(sbase + kOffV + x * kBoxBytes, &tm_v, bar(kBarKvFull), x * 64, n0, h, b);
       }
+      griddep_wait();  // the preprocess has written -lse*log2(e) and D
       int issued0 = 0, issued1 = 0, issued_do = 0;  // completed uses per buffer (for the abort drain)
       for (int u = 0; u < cnt; ++u) {
         const int st = u & 1, use = u >> 1;
@@ -286,52 +294,69 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     regs_inc<kRegsEw>();
     // ---------------------------------------------- elementwise warpgroups
     const int half = warp >> 2;   // 0: query columns [0,64), 1: [64,128)
-    const int wq = warp & 3;      // TMEM lane quadrant
-    const int r = wq * 32 + lane; // KV row within the block
-    const bool kv_valid = (n0 + r) < p.skv;
+    const int wq = warp & 3;      // TMEM lane quadrant: KV rows [32 wq, 32 wq + 32)
+    // S^T and dP^T are read 16 lanes at a time (16x256b): thread t holds KV
+    // rows 32 wq + 16 g + 8 e + t/4 (g, e in {0, 1}) and, in repetition j,
+    // query columns 64 half + 8 j + 2 (t%4) + {0, 1}.  Four threads share a
+    // row and eight column pairs a warp, so the per-column -lse*log2(e) and D
+    // are 16 shared-memory values per thread per block (32 when each thread
+    // owned a whole 64-column row).
+    const int tq = lane & 3;
+    const int tr = lane >> 2;
+    auto kv_row = [&](int g, int e) -> int { return wq * 32 + 16 * g + 8 * e + tr; };
+    bool kv_ok[2][2];
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) kv_ok[g][e] = (n0 + kv_row(g, e)) < p.skv;
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    constexpr uint32_t kLane16 = 16u << 16;
     const uint32_t tS = tmem + lane_base + (uint32_t)(half * 64);
     const uint32_t tdP = tmem + lane_base + 128u + (uint32_t)(half * 64);
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
-    uint8_t* sdS = smem + kOffdS + half * kBoxBytes;
+    const uint32_t sdS = sbase + kOffdS + (uint32_t)half * kBoxBytes;
     bool ok = true;
     for (int u = 0; u < cnt; ++u) {
       const int st = u & 1;
-      const float* snl = reinterpret_cast<const float*>(smem + kOffLse + st * 512) + half * 64;
-      const float* sD = reinterpret_cast<const float*>(smem + kOffD + st * 512) + half * 64;
+      const float* snl = reinterpret_cast<const float*>(smem + kOffLse + st * 512) + half * 64 + 2 * tq;
+      const float* sD = reinterpret_cast<const float*>(smem + kOffD + st * 512) + half * 64 + 2 * tq;
       if (!(ok = mbar_wait(bar(kBarSFull), u & 1, abort_flag, kRoleEw, 5))) break;
       // -lse*log2(e) / D of this block arrived with Q/dO (already complete; this
       // wait makes the bulk-copied bytes visible to these threads)
       if (!(ok = mbar_wait(bar(kBarQFull + st), (u >> 1) & 1, abort_flag, kRoleEw, 1))) break;
       tc_fence_after();
       uint32_t s[2][32];
-      tmem_ld32(tS, s[0]);
-      tmem_ld32(tS + 32, s[1]);
+      tmem_ld_16x256b_x8(tS, s[0]);
+      tmem_ld_16x256b_x8(tS + kLane16, s[1]);
+      uint64_t nl[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 L = *reinterpret_cast<const float2*>(snl + 8 * j);
+        nl[j] = f2_pack(L.x, L.y);
+      }
       tmem_wait_ld();
       reg_fence32(s[0]);
       reg_fence32(s[1]);
-      // P^T = 2^(S^T * scale_log2 + neg_lse_log2[q]) on the MUFU pipe.  Rows past
-      // the K tail are zeroed.
+      // P^T = 2^(S^T * scale_log2 + neg_lse_log2[q]) on the MUFU pipe; rows past
+      // the K tail are zeroed.  P^T goes back to TMEM as bf16 pairs over the
+      // already-read S^T columns (packed column 64 half + 4 j + t%4).
       uint64_t pp[2][16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int g = 0; g < 2; ++g) {
         uint32_t pk[16];
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float4 L = *reinterpret_cast<const float4*>(snl + c * 32 + v * 4);
+        for (int j = 0; j < 8; ++j)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int i = 2 * v + e;
-            const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[c][2 * i]), __uint_as_float(s[c][2 * i + 1])), sl2x2,
-                                      e ? f2_pack(L.z, L.w) : f2_pack(L.x, L.y));
-            pp[c][i] = exp2_mufu2(x);
+            const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[g][4 * j + 2 * e]), __uint_as_float(s[g][4 * j + 2 * e + 1])),
+                                      sl2x2, nl[j]);
+            pp[g][2 * j + e] = exp2_mufu2(x);
             float p0, p1;
-            f2_unpack(pp[c][i], p0, p1);
-            pk[i] = kv_valid ? pack_bf16(p0, p1) : 0u;
+            f2_unpack(pp[g][2 * j + e], p0, p1);
+            pk[2 * j + e] = kv_ok[g][e] ? pack_bf16(p0, p1) : 0u;
           }
-        }
-        tmem_st16(tS + c * 16, pk);
+        tmem_st_16x128b_x8(tS + (g ? kLane16 : 0u), pk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -340,8 +365,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       if (!(ok = mbar_wait(bar(kBarDpFull), u & 1, abort_flag, kRoleEw, 6))) break;
       tc_fence_after();
       uint32_t dp[2][32];
-      tmem_ld32(tdP, dp[0]);
-      tmem_ld32(tdP + 32, dp[1]);
+      tmem_ld_16x256b_x8(tdP, dp[0]);
+      tmem_ld_16x256b_x8(tdP + kLane16, dp[1]);
       tmem_wait_ld();
       reg_fence32(dp[0]);
       reg_fence32(dp[1]);
@@ -349,37 +374,38 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       if (u > 0 && !(ok = mbar_wait(bar(kBarDsEmpty), (u - 1) & 1, abort_flag, kRoleEw, 9))) break;
       const uint64_t m1x2 = f2_pack(-1.f, -1.f);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int g = 0; g < 2; ++g) {
         uint32_t pk[16];
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float4 D = *reinterpret_cast<const float4*>(sD + c * 32 + v * 4);
+        for (int j = 0; j < 8; ++j) {
+          const float2 D = *reinterpret_cast<const float2*>(sD + 8 * j);
+          const uint64_t d2 = f2_pack(D.x, D.y);
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int i = 2 * v + e;
-            const uint64_t dpp = f2_pack(__uint_as_float(dp[c][2 * i]), __uint_as_float(dp[c][2 * i + 1]));
-            const uint64_t t = f2_fma(e ? f2_pack(D.z, D.w) : f2_pack(D.x, D.y), m1x2, dpp);
+            const uint64_t dpp = f2_pack(__uint_as_float(dp[g][4 * j + 2 * e]), __uint_as_float(dp[g][4 * j + 2 * e + 1]));
             float d0, d1;
-            f2_unpack(f2_mul(pp[c][i], t), d0, d1);
-            pk[i] = kv_valid ? pack_bf16(d0, d1) : 0u;
+            f2_unpack(f2_mul(pp[g][2 * j + e], f2_fma(d2, m1x2, dpp)), d0, d1);
+            pk[2 * j + e] = kv_ok[g][e] ? pack_bf16(d0, d1) : 0u;
+            // row of dS^T in shared memory for the dQ MMA (128B-swizzled
+            // [kv][q] box of this half): 4 bytes of the 16-byte chunk j
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(sdS + sw128_offset((uint32_t)kv_row(g, e), (uint32_t)j) +
+                                                          4u * (uint32_t)tq),
+                         "r"(pk[2 * j + e])
+                         : "memory");
           }
         }
-        // dS^T as the A operand of the dK MMA: bf16 pairs over this warpgroup's
-        // (already read) dP^T columns
-        tmem_st16(tdP + c * 16, pk);
-        // row r of dS^T in shared memory for the dQ MMA, query columns
-        // [64*half + 32c, +32): 4 chunks of 16 B
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const uint32_t off = sw128_offset((uint32_t)r, (uint32_t)(c * 4 + v));
-          *reinterpret_cast<uint4*>(sdS + off) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-        }
+        // dS^T as the A operand of the dK MMA: bf16 pairs over this
+        // warpgroup's (already read) dP^T columns
+        tmem_st_16x128b_x8(tdP + (g ? kLane16 : 0u), pk);
       }
       fence_proxy_async_smem();
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kBarDsReady));
     }
+    // the epilogue reads dV / dK rows 32 x 32b: thread = one KV row
+    const int r = wq * 32 + lane;
+    const bool kv_valid = (n0 + r) < p.skv;
     // ----------------------------------------------------------- epilogue
     // WG A writes dV (unscaled), WG B writes dK (scaled by softmax_scale)
     if (ok) ok = mbar_wait(bar(kBarDkvFull), 0, abort_flag, kRoleEpi, 12);
@@ -451,6 +477,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     const uint32_t sx = sbase + kOffX;
     uint8_t* xb = smem + kOffX;
     const bool leader = (threadIdx.x == 256);
+    if (leader) griddep_wait();  // the preprocess has zeroed dq_accum
     int* const q_sem = p.deterministic ? p.dq_sem + bh * (size_t)p.m_blocks : nullptr;
     for (int u = 0; u < cnt; ++u) {
       if (!mbar_wait(bar(kBarDqFull), u & 1, abort_flag, kRoleDq, 10)) break;

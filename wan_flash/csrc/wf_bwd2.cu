@@ -183,6 +183,9 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // programmatic dependent of the preprocess (as the single-CTA kernel):
+  // -lse*log2(e), D and dq_accum only after griddep_wait()
+  griddep_launch_dependents();
   const bool leader = (rank == 0);
   auto lbar = [&](int i) -> uint32_t { return mapa_shared(bar(i), 0); };  // the leader's barrier
 
@@ -243,6 +246,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
         tma_load_4d_pair(sbase + kOffV + x * kBox, &tm_v, lbar(kBarKvFull), x * 64, n0, h, b);
         tma_load_4d_pair(sbase + kOffKd + x * kBox, &tm_k, lbar(kBarKvFull), dh, pair_n0 + 128 * x, h, b);
       }
+      griddep_wait();  // the preprocess has written -lse*log2(e) and D
       int lse_issued[2] = {0, 0};
       bool ok = true;
       for (int u = 0; u < cnt && ok; ++u) {
@@ -519,6 +523,7 @@ __global__ void __launch_bounds__(bwd2::kThreads, 1)
     const uint32_t sx = sbase + kOffX;
     uint8_t* xb = smem + kOffX;
     const bool lead_thr = (threadIdx.x == 256);
+    if (lead_thr) griddep_wait();  // the preprocess has zeroed dq_accum
     const uint32_t drained = lbar(kBarDqDrained);
     for (int u = 0; u < cnt; ++u) {
       if (!mbar_wait(bar(kBarDqFull), u & 1, abort_flag, kRoleDq2, 15)) break;

@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "wan_flash.h"
 #include "wf_common.cuh"
@@ -118,6 +119,37 @@ int check_dims(int b, int s1, int s2, int h) {
   if ((double)s1 * h * 256.0 >= 1099511627776.0 || (double)s2 * h * 256.0 >= 1099511627776.0)
     return fail(WF_ERR_UNSUPPORTED, "sequence too long for a TMA stride");
   return WF_OK;
+}
+
+// Launch through cudaLaunchKernelEx with programmatic stream serialization
+// (programmatic dependent launch: the kernel may start while the previous
+// kernel of the stream finishes; it calls griddep_wait() before touching that
+// kernel's results) and, for cluster_x > 1, a 1-D cluster.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  lc.attrs = attr;
+  lc.numAttrs = n;
+  return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
 }
 
 int launch_check(const char* what) {
@@ -324,6 +356,7 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
   const int cluster_n = cfg ? cfg->cluster_n : 0;
   if (cluster_n < 0 || cluster_n > 2) return fail(WF_ERR_INVALID_ARG, "cluster_n=%d must be 0 (auto), 1 or 2", cluster_n);
   const int deterministic = cfg ? cfg->deterministic : 0;
+  const bool pdl = !(cfg && cfg->pdl_off);
   if (deterministic && (!cfg->sem || (reinterpret_cast<uintptr_t>(cfg->sem) & 3)))
     return fail(WF_ERR_INVALID_ARG, "deterministic mode needs a 4-byte aligned sem workspace");
   if (deterministic && cluster_n == 2)
@@ -360,9 +393,8 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
   if (!use_pair) {
     p.n_blocks_padded = p.n_blocks;
     dim3 grid(p.n_blocks * splits, h, b);
-    wf_bwd_main_kernel<<<grid, kBwdThreads, bwd_smem_bytes(), reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv,
-                                                                                                         mdo, p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_ex(wf_bwd_main_kernel, grid, dim3(kBwdThreads), bwd_smem_bytes(),
+                              reinterpret_cast<cudaStream_t>(stream), pdl, 1u, mq, mk, mv, mdo, p);
     if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_main launch");
     return launch_check("wf_bwd_main launch");
   }
@@ -371,19 +403,9 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
   if ((rc = make_bshd_map(&mq64, q, b, sq, h, 64)) || (rc = make_bshd_map(&mdo64, dO, b, sq, h, 64))) return rc;
   const int n_pairs = (p.n_blocks + 1) / 2;
   p.n_blocks_padded = 2 * n_pairs;
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(2 * n_pairs * splits, h, b);
-  lc.blockDim = dim3(kBwdThreads, 1, 1);
-  lc.dynamicSmemBytes = bwd2_smem_bytes();
-  lc.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&lc, wf_bwd2_main_kernel, mq, mq64, mk, mv, mdo, mdo64, p);
+  cudaError_t e = launch_ex(wf_bwd2_main_kernel, dim3(2 * n_pairs * splits, h, b), dim3(kBwdThreads),
+                            bwd2_smem_bytes(), reinterpret_cast<cudaStream_t>(stream), pdl, 2u, mq, mq64, mk, mv, mdo,
+                            mdo64, p);
   if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_main (pair) launch");
   return launch_check("wf_bwd_main (pair) launch");
 }
@@ -398,8 +420,10 @@ int wf_bwd_convert(const float* accum, void* out, float scale, int b, int s, int
   if ((rc = device_setup(&dev))) return rc;
   const int s_rounded = (s + 127) / 128 * 128;
   dim3 grid(s_rounded / 32, h, b);
-  wf_convert_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      accum, reinterpret_cast<__nv_bfloat16*>(out), scale, s, s_rounded, h);
+  // a programmatic dependent of the kernel that filled `accum`
+  cudaError_t e = launch_ex(wf_convert_kernel, grid, dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), true, 1u,
+                            accum, reinterpret_cast<__nv_bfloat16*>(out), scale, s, s_rounded, h);
+  if (e != cudaSuccess) return cuda_fail(e, "wf_bwd_convert launch");
   return launch_check("wf_bwd_convert launch");
 }
 

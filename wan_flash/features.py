@@ -48,6 +48,13 @@ Backward flags
                           are added in KV-block (split) order behind
                           per-block counters, so every gradient is bitwise
                           reproducible; slower, single-CTA kernel only.
+  pdl                     True (default): the main kernel and the converts are
+                          launched as programmatic dependents of the kernel
+                          before them (the reference's use_pdl=True,
+                          bwd_sm90.py:140,498,506): their set-up and the K/V
+                          loads overlap the previous kernel's tail, and each
+                          waits (griddepcontrol.wait) before reading its
+                          results.  False launches the main kernel plainly.
 """
 
 from dataclasses import dataclass, replace
@@ -74,6 +81,7 @@ class BwdFeatures:
     nsplit: int = 0
     cluster_n: int = 1
     deterministic: bool = False
+    pdl: bool = True
 
 
 _current = FwdFeatures()

@@ -133,7 +133,7 @@ def bwd_plan(b: int, sq: int, skv: int, h: int, sms: int | None = None) -> dict:
     return {
         "sq_rounded": sq_rounded, "m_blocks": m_blocks, "n_blocks": n_blocks,
         "skv_rounded": skv_rounded, "nsplit": nsplit, "cluster_n": f.cluster_n,
-        "deterministic": bool(f.deterministic),
+        "deterministic": bool(f.deterministic), "pdl": bool(f.pdl),
         # deterministic mode: ordered-accumulation counters, (b*h) x (m_blocks + n_blocks) int32
         "sem_len": b * h * (m_blocks + n_blocks) if f.deterministic else 0,
     }
@@ -218,6 +218,7 @@ def _bwd_multi(q, contexts, do, marks=None):
             else:
                 dk_accum = dv_accum = None
             cfg = _lib.BwdCfg(plan["nsplit"], plan["cluster_n"])
+            cfg.pdl_off = 0 if plan["pdl"] else 1
             sem = None
             if plan["deterministic"]:
                 sem = torch.zeros(plan["sem_len"], device=dev, dtype=torch.int32)
