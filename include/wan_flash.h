@@ -52,6 +52,14 @@ typedef struct wf_fwd_cfg {
                               1 = one CTA per 256-row work item,
                               2 = persistent (min(items, num_sms) CTAs)      */
   int num_sms;             /* persistent grid size; 0 = the device's SMs     */
+  int cluster_m;           /* 0 = auto (2 for one KV context on the
+                              one-item-per-CTA schedule, else 1),
+                              1 = one CTA per 256-row work item,
+                              2 = CTA pairs along the query axis (cluster of
+                              2, 2-SM tensor-core MMAs, each CTA loading half
+                              of every K/V tile: the reference's cluster
+                              (2, 1) without multicast loads); one KV context
+                              and the one-item-per-CTA schedule only        */
 } wf_fwd_cfg;
 
 /* Backward options (mirror BwdFeatures, wan_flash/features.py:45-70). */

@@ -159,3 +159,51 @@ def test_fwd_deterministic():
     a = wan_flash_fwd(qc, kc, vc)
     b = wan_flash_fwd(qc, kc, vc)
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+# CTA pairs (cluster_mn (2, 1)) run on the one-item-per-CTA schedule: sizes
+# covering a cluster whose second CTA lies wholly past sq (sq <= 256 rows per
+# cluster half), ragged query and key tails, tails of at most 64 keys, b > 1
+PAIR_SHAPES = [(1, 1, 1, 1), (1, 1, 300, 300), (1, 2, 512, 1000), (1, 2, 700, 257), (2, 3, 1100, 520),
+               (1, 1, 1500, 65), (1, 2, 2048, 2048), (1, 1, 257, 8300)]
+
+
+@pytest.mark.parametrize("b,h,sq,skv", PAIR_SHAPES, ids=lambda x: str(x))
+def test_fwd_cta_pair(b, h, sq, skv):
+    """The CTA-pair forward against the oracle, and against the single-CTA
+    forward of the same inputs (same arithmetic up to the MMA's summation
+    order)."""
+    from wan_flash import _lib, features
+    from wan_flash.interface import wan_flash_fwd
+
+    q, k, v, _ = seeded(b, sq, skv, h, seed=b * 7 + h * 5 + sq + skv)
+    try:
+        features.set_overrides(scheduler="single", cluster_mn=(2, 1))
+        o, lse, e, lse_err = fwd_vs_oracle(q, k, v)
+        assert_fwd_ok(e, lse_err, f"pair {b}x{h}x{sq}x{skv}")
+        features.set_overrides(cluster_mn=(1, 1))
+        qc, kc, vc = (t.cuda() for t in (q, k, v))
+        o1, l1 = wan_flash_fwd(qc, kc, vc)
+        _lib.check_device()
+    finally:
+        features.reset()
+    assert float((o.float() - o1.float()).abs().max()) <= 2e-2
+    assert float((lse - l1).abs().max()) <= 1e-5
+
+
+def test_fwd_cta_pair_rejected_where_unsupported():
+    """cluster_m = 2 is refused (not silently changed) with the persistent
+    schedule or two KV contexts."""
+    import ctypes
+
+    from wan_flash import _lib
+
+    q, k, v, _ = seeded(1, 256, 512, 1, seed=1)
+    qc, kc, vc = (t.cuda() for t in (q, k, v))
+    o = torch.empty_like(qc)
+    lse = torch.empty(1, 1, 256, device="cuda")
+    cfg = _lib.FwdCfg(8.0, 2, 0, 2)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rc = _lib.lib().wf_fwd(P(qc), P(kc), P(vc), P(o), P(lse), 1, 256, 512, 1, ctypes.byref(cfg),
+                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == -2  # WF_ERR_UNSUPPORTED

@@ -70,7 +70,7 @@ def test_features_defaults_overrides_and_validation():
         features.set_bwd_overrides(nsplit=3)
         assert features.get_bwd().nsplit == 3
         with pytest.raises(ValueError):
-            features.set_overrides(cluster_mn=(2, 1))  # no multicast in this build
+            features.set_overrides(cluster_mn=(1, 2))  # CTA pairs run along the query axis only
         with pytest.raises(ValueError):
             features.set_bwd_overrides(tile_m=80)
         with pytest.raises(ValueError):
@@ -81,6 +81,8 @@ def test_features_defaults_overrides_and_validation():
             features.set_overrides(num_sms=-1)
         features.set_overrides(scheduler="auto", num_sms=0)
         # a rejected override leaves the state unchanged
+        assert features.get().cluster_mn == (2, 1)
+        features.set_overrides(cluster_mn=(1, 1))
         assert features.get().cluster_mn == (1, 1)
         # backward kernel form: single CTAs (default) or CTA pairs
         assert features.get_bwd().cluster_n == 1

@@ -34,7 +34,8 @@ EXPORTS = (
 
 
 class FwdCfg(ctypes.Structure):
-    _fields_ = [("rescale_threshold", ctypes.c_float), ("scheduler", ctypes.c_int), ("num_sms", ctypes.c_int)]
+    _fields_ = [("rescale_threshold", ctypes.c_float), ("scheduler", ctypes.c_int), ("num_sms", ctypes.c_int),
+                ("cluster_m", ctypes.c_int)]
 
 
 class BwdCfg(ctypes.Structure):

@@ -19,7 +19,7 @@ PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libwanflash.so"
-SOURCES = ["wf_lib.cu", "wf_capi.cu", "wf_fwd.cu", "wf_bwd.cu", "wf_bwd2.cu", "wf_aux.cu", "wf_noalloc.cu", "wf_common.cuh",
+SOURCES = ["wf_lib.cu", "wf_capi.cu", "wf_fwd.cu", "wf_fwd2.cu", "wf_bwd.cu", "wf_bwd2.cu", "wf_aux.cu", "wf_noalloc.cu", "wf_common.cuh",
            "wf_kernels.h"]
 
 NVCC_FLAGS = [

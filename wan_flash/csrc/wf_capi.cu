@@ -84,6 +84,8 @@ int device_setup(int* dev_out) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd narrow smem)");
   e = cudaFuncSetAttribute(wf_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd dual smem)");
+  e = cudaFuncSetAttribute(wf_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd2_smem_bytes());
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fwd pair smem)");
   e = cudaFuncSetAttribute(wf_bwd_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem_bytes());
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bwd smem)");
   e = cudaFuncSetAttribute(wf_bwd2_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd2_smem_bytes());
@@ -229,6 +231,21 @@ static int fwd_launch(const void* q, int n_ctx, const void* const* k, const void
   const bool persistent = sched == 2 || (sched == 0 && total_blocks <= kFwdPersistMaxBlocks);
   const int grid = persistent ? (int)std::min<long long>(n_items, sms) : p.n_items;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int cluster_m = cfg ? cfg->cluster_m : 0;
+  if (cluster_m < 0 || cluster_m > 2) return fail(WF_ERR_INVALID_ARG, "cluster_m %d not in {0, 1, 2}", cluster_m);
+  if (cluster_m == 2 && (n_ctx != 1 || persistent))
+    return fail(WF_ERR_UNSUPPORTED, "cluster_m = 2 needs one KV context and the one-item-per-CTA schedule");
+  if (n_ctx == 1 && !persistent && (cluster_m == 2 || (cluster_m == 0 && kFwdPairDefault))) {
+    // CTA pairs: one cluster of 2 per 512 query rows of a (batch, head)
+    CUtensorMap mk64;
+    if ((rc = make_bshd_map(&mk64, k[0], b, skv[0], h, 64))) return rc;
+    const long long n_cl = (long long)((p.n_pairs + 1) / 2) * h * b;
+    if (2 * n_cl > 0x7fffffffLL) return fail(WF_ERR_UNSUPPORTED, "%lld clusters exceed the grid limit", n_cl);
+    cudaError_t e = launch_ex(wf_fwd2_kernel, dim3((unsigned)(2 * n_cl)), dim3(kFwdThreads), fwd2_smem_bytes(), st,
+                              false, 2u, mq, mk64, mv[0], mo[0], p);
+    if (e != cudaSuccess) return cuda_fail(e, "wf_fwd pair launch");
+    return launch_check("wf_fwd pair launch");
+  }
   const size_t smem = fwd_smem_bytes();
   if (n_ctx == 2)
     wf_fwd_kernel<2><<<grid, kFwdThreads, smem, st>>>(mq, mk[0], mv[0], mo[0], mk[1], mv[1], mo[1], p);

@@ -459,6 +459,35 @@ __device__ __forceinline__ void mma_commit_e(uint32_t bar) {
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
       : "memory");
 }
+// CTA-pair forms with the elected lane's predicate inside the asm block
+// (converged MMA warp of the leader CTA).
+__device__ __forceinline__ void mma_ss_pair_ee(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_pair_ee(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair_ee(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
+          bar),
+      "h"(cta_mask)
+      : "memory");
+}
 __device__ __forceinline__ void mma_ss_pair_e(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
   if (elect_one()) mma_ss_pair(d, a, b, id, acc);
 }

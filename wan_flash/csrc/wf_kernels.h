@@ -43,6 +43,9 @@ __global__ void wf_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __
                               const __grid_constant__ CUtensorMap tm_v0, const __grid_constant__ CUtensorMap tm_o0,
                               const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_v1,
                               const __grid_constant__ CUtensorMap tm_o1, FwdParams p);
+__global__ void wf_fwd2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k64,
+                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                               FwdParams p);
 __global__ void wf_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                                    BwdParams p);
@@ -58,9 +61,13 @@ __global__ void wf_convert_kernel(const float* __restrict__ accum, __nv_bfloat16
                                   int s, int s_rounded, int h);
 
 size_t fwd_smem_bytes();
+size_t fwd2_smem_bytes();
 size_t bwd_smem_bytes();
 size_t bwd2_smem_bytes();
 
+// wf_fwd with cluster_m = 0 (auto), one KV context, one item per CTA: true =
+// the CTA-pair kernel.
+constexpr bool kFwdPairDefault = true;
 // wf_bwd_main with cluster_n = 0 (auto): true = the CTA-pair kernel.
 constexpr bool kBwdPairDefault = false;
 

@@ -3,6 +3,7 @@
 // (no relocatable device code or device link step needed).
 #include "wf_capi.cu"
 #include "wf_fwd.cu"
+#include "wf_fwd2.cu"
 #include "wf_bwd.cu"
 #include "wf_bwd2.cu"
 #include "wf_aux.cu"

@@ -19,8 +19,16 @@ Forward flags
   num_sms                 persistent grid size; 0 = the device's SM count.
   tile_m / tile_n         fixed at 128 x 128 (two 128-row query tiles per CTA).
   num_stages              K/V ring depth in (K, V) pairs (fixed at 2).
-  cluster_mn              (1, 1) only: no TMA multicast anywhere (multi-GPU
-                          runs must never issue multicast loads on this pool).
+  cluster_mn              (2, 1) (default): pairs of CTAs along the query axis
+                          (cluster of 2) issue 2-SM tensor-core MMAs
+                          (M = 256): each CTA supplies its own query rows
+                          and loads half of every K/V tile, where the
+                          reference's cluster (2, 1) multicasts whole K/V
+                          tiles into both CTAs.  Used for one KV context on
+                          the one-item-per-CTA schedule (long self
+                          attention); the persistent and two-context paths
+                          run single CTAs.  (1, 1): single CTAs everywhere.
+                          No TMA load is multicast in either form.
   intra_wg_overlap        the two query tiles of a CTA ping-pong softmax and
                           tensor work (always on in this design).
   mma_pv_is_rs            P feeds the PV MMA from tensor memory (always on).
@@ -69,7 +77,7 @@ class FwdFeatures:
     tile_m: int = 128
     tile_n: int = 128
     scheduler: str = "auto"
-    cluster_mn: tuple = (1, 1)
+    cluster_mn: tuple = (2, 1)
     num_sms: int = 0
 
 
@@ -93,8 +101,8 @@ def _validate_fwd(f: FwdFeatures):
         raise ValueError("the sm_100a forward is built for 128x128 tiles")
     if f.num_stages != 2:
         raise ValueError("the forward K/V ring holds 2 (K, V) pairs")
-    if tuple(f.cluster_mn) != (1, 1):
-        raise ValueError("cluster_mn must be (1, 1): this build issues no multicast TMA loads")
+    if tuple(f.cluster_mn) not in ((1, 1), (2, 1)):
+        raise ValueError("cluster_mn must be (2, 1) (CTA pairs along the query axis) or (1, 1)")
     if f.scheduler not in ("auto", "single", "persistent"):
         raise ValueError(f"unknown scheduler {f.scheduler!r}")
     if f.num_sms < 0:

@@ -65,6 +65,14 @@ def _mark(marks, name):
         marks.append((name, ev))
 
 
+def _fwd_cfg(f) -> "_lib.FwdCfg":
+    """wf_fwd_cfg from the forward feature flags.  cluster_mn (2, 1) maps to
+    cluster_m = 0 (auto: CTA pairs where the kernel supports them, single
+    CTAs elsewhere), (1, 1) to single CTAs."""
+    return _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler],
+                       int(f.num_sms), 0 if tuple(f.cluster_mn) == (2, 1) else 1)
+
+
 def wan_flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     return _fwd_impl(q, k, v)
 
@@ -86,8 +94,7 @@ def _fwd_impl(q, k, v, marks=None):
         return o, lse
 
     f = features.get()
-    cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler],
-                      int(f.num_sms))
+    cfg = _fwd_cfg(f)
     with torch.cuda.device(q.device):
         _mark(marks, "fwd")
         rc = _lib.lib().wf_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), b, sq, skv, h,
@@ -264,8 +271,7 @@ def wan_flash_fwd_dual(q: torch.Tensor, k0: torch.Tensor, v0: torch.Tensor, k1: 
     if o0.numel() == 0:
         return o0, lse0, o1, lse1
     f = features.get()
-    cfg = _lib.FwdCfg(float(f.rescale_skip_threshold), {"auto": 0, "single": 1, "persistent": 2}[f.scheduler],
-                      int(f.num_sms))
+    cfg = _fwd_cfg(f)
     with torch.cuda.device(q.device):
         rc = _lib.lib().wf_fwd_dual(_ptr(q), _ptr(k0), _ptr(v0), _ptr(k1), _ptr(v1), _ptr(o0), _ptr(o1),
                                     _ptr(lse0), _ptr(lse1), b, sq, k0.shape[1], k1.shape[1], h,
