@@ -471,6 +471,7 @@ def run_features_ab(args):
         ("fwd", "rescale_skip_threshold=0", {"rescale_skip_threshold": 0.0}, {}),
         ("fwd", "scheduler=single", {"scheduler": "single"}, {}),
         ("fwd", "scheduler=persistent", {"scheduler": "persistent"}, {}),
+        ("fwd", "cluster_mn=(1,1)", {"cluster_mn": (1, 1)}, {}),
         ("bwd", "defaults", {}, {}),
         ("bwd", "cluster_n=2", {}, {"cluster_n": 2}),
         ("bwd", "deterministic", {}, {"deterministic": True}),
