@@ -74,11 +74,11 @@ C5_CONTEXT = 512
 DUAL_IMAGE_CONTEXT = 257
 METRIC = "fwd and bwd TFLOP/s per B200 at Wan shapes; % of bf16 dense peak; 1/2/4/8-GPU"
 # DRAM bytes (read + write) per launch per head, from one ncu capture of the
-# C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd_c2_h4.md);
+# C2 shape at 4 heads (profiles/wf_bwd_main_c2_h4.md, profiles/wf_fwd2_c2_h4.md);
 # traffic grows with the number of heads, so it is scaled by the run's heads.
-DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): 318.49e6 / 4, ("c2", "fwd"): 118.96e6 / 4,
+DRAM_BYTES_PER_HEAD = {("c2", "bwd_main"): (219.57e6 + 102.19e6) / 4, ("c2", "fwd"): (103.67e6 + 16.50e6) / 4,
                        # C4 shape at 4 heads (profiles/dram_c4_h4.md)
-                       ("c4", "bwd_main"): (1223.91e6 + 642.02e6) / 4, ("c4", "fwd"): (263.62e6 + 63.04e6) / 4}
+                       ("c4", "bwd_main"): (1232.46e6 + 625.67e6) / 4, ("c4", "fwd"): (270.61e6 + 63.98e6) / 4}
 NOMINAL_BF16_TFLOPS = 2250.0
 
 
