@@ -482,8 +482,21 @@ def run_features_ab(args):
         settings.append(("bwd", f"nsplit={n}", {}, {"nsplit": n}))
     times = {i: [] for i in range(len(settings))}
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fwd_idx = [i for i, st in enumerate(settings) if st[0] == "fwd"]
+    bwd_idx = [i for i, st in enumerate(settings) if st[0] == "bwd"]
     for rnd_i in range(args.warmup + args.steps):
-        for i, (what, _, fo, bo) in enumerate(settings):
+        # each round runs the forward settings, one untimed backward (so the
+        # first timed backward does not inherit the forward runs' power and
+        # clock state), then the backward settings; both blocks are rotated by
+        # the round index so no setting always runs first
+        rf, rb = rnd_i % len(fwd_idx), rnd_i % len(bwd_idx)
+        order = fwd_idx[rf:] + fwd_idx[:rf] + [None] + bwd_idx[rb:] + bwd_idx[:rb]
+        for i in order:
+            if i is None:
+                features.reset()
+                interface.wan_flash_bwd(q, k, v, o, lse, do)
+                continue
+            what, _, fo, bo = settings[i]
             features.reset()
             features.set_overrides(**fo)
             features.set_bwd_overrides(**bo)
