@@ -170,9 +170,10 @@ PAIR_SHAPES = [(1, 1, 1, 1), (1, 1, 300, 300), (1, 2, 512, 1000), (1, 2, 700, 25
 
 @pytest.mark.parametrize("b,h,sq,skv", PAIR_SHAPES, ids=lambda x: str(x))
 def test_fwd_cta_pair(b, h, sq, skv):
-    """The CTA-pair forward against the oracle, and against the single-CTA
-    forward of the same inputs (same arithmetic up to the MMA's summation
-    order)."""
+    """The CTA-pair forward against the oracle, and bitwise against the
+    single-CTA forward of the same inputs: each SM computes its own query
+    rows with the same K-step order, the pair only splits the B operand's
+    columns (keys for S, head dims for O) between the two SMs."""
     from wan_flash import _lib, features
     from wan_flash.interface import wan_flash_fwd
 
@@ -187,8 +188,7 @@ def test_fwd_cta_pair(b, h, sq, skv):
         _lib.check_device()
     finally:
         features.reset()
-    assert float((o.float() - o1.float()).abs().max()) <= 2e-2
-    assert float((lse - l1).abs().max()) <= 1e-5
+    assert torch.equal(o, o1) and torch.equal(lse, l1)
 
 
 def test_fwd_cta_pair_rejected_where_unsupported():
