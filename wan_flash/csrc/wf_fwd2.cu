@@ -180,6 +180,14 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
         }
         if (!ok) break;
       }
+      if (*abort_flag && leader) {
+        // drain: every copy either CTA issued completes on the leader's
+        // barriers, so once these phases complete no copy is in flight into
+        // either CTA (the peer waits at the closing cluster barrier)
+        for (int t = 0; t < 2; ++t) mbar_wait_drain(bar(kBarQFull + t), 0);
+        for (int sl = 0; sl < kSlots && sl < u; ++sl)  // u units were issued; slot sl took the last of its uses
+          mbar_wait_drain(bar(kBarKvFull + sl), ((u - 1 - sl) / kSlots) & 1);
+      }
     }
   } else if (warp == 8) {
     regs_dec<kRegsOther>();
