@@ -128,13 +128,19 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   const int m_begin = split * p.m_chunk;
   const int m_end = min(m_begin + p.m_chunk, p.m_blocks);
   const int cnt = m_end - m_begin;
-  // Query blocks in natural order: the CTAs of a head resident at the same
-  // time walk the same Q/dO tiles together, so each tile is fetched from
-  // HBM about once and served to the others from L2.  (A walk rotated by the
-  // KV block index, which spreads the dQ reductions over more lines,
-  // measured 1-2 % slower.)  Deterministic mode relies on this order: KV
-  // block nb meets each query block just after KV block nb-1.
-  auto qblock = [&](int u) -> int { return m_begin + u; };
+  // The CTAs of a head resident at the same time walk the same Q/dO tiles
+  // together, so each tile is fetched from HBM about once and served to the
+  // others from L2.  Successive waves (one CTA per SM, `p.wave` CTAs) walk in
+  // alternating directions: a wave starts on the query blocks whose Q/dO
+  // tiles and dQ accumulator lines the previous wave touched last, which are
+  // still in L2.  (A walk rotated by the KV block index, spreading the dQ
+  // reductions over more lines, measured 1-2 % slower.)  Deterministic mode
+  // walks every CTA forwards: it relies on KV block nb meeting each query
+  // block just after KV block nb-1.  A CTA's direction depends only on its
+  // grid position, so dK/dV stay bitwise reproducible at nsplit = 1.
+  const unsigned lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const bool reverse = !p.deterministic && p.wave > 0 && ((lin / (unsigned)p.wave) & 1u);
+  auto qblock = [&](int u) -> int { return reverse ? m_end - 1 - u : m_begin + u; };
   if (cnt <= 0) return;  // empty split: nothing to add (uniform for the CTA)
   const size_t bh = (size_t)b * p.h + h;
 

@@ -399,6 +399,7 @@ int wf_bwd_main(const void* q, const void* k, const void* v, const void* dO, con
   p.scale = (float)(1.0 / std::sqrt(128.0));
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
   p.deterministic = deterministic ? 1 : 0;
+  p.wave = g_dev_sms[dev];
   p.dq_sem = deterministic ? cfg->sem : nullptr;
   p.dkv_sem = deterministic ? cfg->sem + (size_t)b * h * p.m_blocks : nullptr;
   CUtensorMap mq, mk, mv, mdo;

@@ -36,6 +36,7 @@ struct BwdParams {
   int* dq_sem;             // deterministic: (b*h, m_blocks) dQ contributions added so far
   int* dkv_sem;            // deterministic, split-M: (b*h, n_blocks) splits added so far
   int deterministic;
+  int wave;                // CTAs resident at once (one per SM): the serpentine walk's period
 };
 
 template <int kMode>
