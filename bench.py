@@ -522,6 +522,46 @@ def run_features_ab(args):
         print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- output check
+def timed_output_check(q, k, v, do, o, dq, dk, dv, lse, rows: int = 1024) -> dict:
+    """Compare the last timed step's outputs with plain fp32 attention
+    (torch matmuls, TF32 off) on slices of head 0 of batch 0: O, LSE and dQ
+    of query rows [0, rows), dK and dV of key rows [0, rows).  The backward
+    reference recomputes P from the kernel's own lse and uses its o, as the
+    reference's tests do.  Returns rel_l2 errors and the LSE max abs error."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        with torch.no_grad():
+            scale = 1.0 / math.sqrt(q.shape[-1])
+            qh, kh, vh, doh, oh = (t[0, :, 0].float() for t in (q, k, v, do, o))
+            lh = lse[0, 0].float()
+            rq, rk = min(rows, qh.shape[0]), min(rows, kh.shape[0])
+
+            def rel(x, y):
+                return float((x.float() - y).norm() / y.norm().clamp_min(1e-30))
+
+            s_r = (qh[:rq] @ kh.T) * scale
+            lse_ref = torch.logsumexp(s_r, dim=-1)
+            o_ref = torch.softmax(s_r, dim=-1) @ vh
+            p_r = torch.exp(s_r - lh[:rq, None])
+            d_r = (doh[:rq] * oh[:rq]).sum(-1)
+            dq_ref = (p_r * ((doh[:rq] @ vh.T) - d_r[:, None])) @ kh * scale
+            del s_r, p_r
+            s_c = (qh @ kh[:rk].T) * scale
+            p_c = torch.exp(s_c - lh[:, None])
+            dv_ref = p_c.T @ doh
+            d_all = (doh * oh).sum(-1)
+            dk_ref = (p_c * ((doh @ vh[:rk].T) - d_all[:, None])).T @ qh * scale
+            return {"o_rel_l2": rel(o[0, :rq, 0], o_ref), "lse_max_abs": float((lh[:rq] - lse_ref).abs().max()),
+                    "dq_rel_l2": rel(dq[0, :rq, 0], dq_ref), "dk_rel_l2": rel(dk[0, :rk, 0], dk_ref),
+                    "dv_rel_l2": rel(dv[0, :rk, 0], dv_ref)}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -623,7 +663,7 @@ def main():
             return o0, dq, grads
         o, lse = interface._fwd_impl(q, k, v, marks)
         dq, dk, dv = interface._bwd_impl(q, k, v, o, lse, do, marks)
-        return o, dq, dk, dv
+        return o, dq, dk, dv, lse
 
     def barrier():
         if world > 1:
@@ -650,15 +690,32 @@ def main():
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record()
+    last = None
     for _ in range(args.steps):
         marks = []
-        step(marks)
+        last = step(marks)
         all_marks.append(marks)
     t_end.record()
     barrier()
     ms = t_start.elapsed_time(t_end)
     ms = max_over_ranks(ms)
     ms_per_step = ms / args.steps
+    # the last timed step's outputs against fp32 attention on slices of head 0
+    # (outside the timed region; every rank checks its own heads' slice)
+    timed_check = None
+    if not dual:
+        errs = timed_output_check(q, k, v, do, *last)
+        t_err = torch.tensor(list(errs.values()), device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t_err, op=dist.ReduceOp.MAX)
+        timed_check = dict(zip(errs.keys(), t_err.tolist()))
+        timed_check.update({"tolerance_rel_l2": 4.5e-3, "tolerance_lse_abs": 1e-5,
+                            "ok": all(timed_check[n] <= 4.5e-3 for n in ("o_rel_l2", "dq_rel_l2", "dk_rel_l2",
+                                                                          "dv_rel_l2"))
+                            and timed_check["lse_max_abs"] <= 1e-5,
+                            "against": "fp32 torch attention of head 0: query rows [0, 1024) for o/lse/dq, "
+                                       "key rows [0, 1024) for dk/dv (o and lse of the kernel given to the "
+                                       "backward, as the reference's tests do)"})
 
     # per-kernel averages from the marks of the timed region
     per = {}
@@ -838,6 +895,7 @@ def main():
             "clocks": clk,
             "gpu_launches": launches_per_step * args.steps,
             "sp_block": sp_block,
+            "timed_outputs_check": timed_check,
             "bwd_nsplit": plan["nsplit"],
             "bwd_cluster_n": plan["cluster_n"],
         }

@@ -67,3 +67,30 @@ def test_reference_arm_uses_all_cores_and_the_same_config():
     assert line["impl"] == "reference" and line["config"] == bench.config_dict("c4", 1)
     assert line["cpu_baseline"]["cores"] == os.cpu_count()
     assert line["scaling"] == "strong" and line["value"] > 0
+
+
+def test_timed_output_check_against_the_oracle():
+    """The bench's post-timing check of its outputs (fp32 torch attention on
+    slices of head 0) accepts the oracle's own outputs and flags a corrupted
+    gradient; it runs on the host here."""
+    import numpy as np
+    import torch
+
+    from oracle.oracle import oracle_bwd, oracle_fwd
+    from tests.helpers import make_inputs, to_bhsd_f32
+
+    bench = _bench()
+    q, k, v, do = make_inputs(1, 96, 80, 2, seed=11)
+
+    def bshd(x):  # (b, h, s, d) numpy -> (b, s, h, d) bf16 torch
+        return torch.from_numpy(np.ascontiguousarray(x)).transpose(1, 2).contiguous().to(torch.bfloat16)
+
+    o, lse = oracle_fwd(to_bhsd_f32(q), to_bhsd_f32(k), to_bhsd_f32(v))
+    o_t = bshd(o)
+    lse_t = torch.from_numpy(lse).float()
+    dq, dk, dv = oracle_bwd(to_bhsd_f32(q), to_bhsd_f32(k), to_bhsd_f32(v), to_bhsd_f32(o_t), lse, to_bhsd_f32(do))
+    errs = bench.timed_output_check(q, k, v, do, o_t, bshd(dq), bshd(dk), bshd(dv), lse_t, rows=64)
+    assert all(errs[n] <= 4.5e-3 for n in ("o_rel_l2", "dq_rel_l2", "dk_rel_l2", "dv_rel_l2")), errs
+    assert errs["lse_max_abs"] <= 1e-5, errs
+    bad = bshd(dk) * 1.01
+    assert bench.timed_output_check(q, k, v, do, o_t, bshd(dq), bad, bshd(dv), lse_t, rows=64)["dk_rel_l2"] > 4.5e-3
