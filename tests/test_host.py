@@ -97,6 +97,29 @@ def test_features_defaults_overrides_and_validation():
     assert features.get_bwd() == features.BwdFeatures()
 
 
+def test_fwd_cfg_matches_c_struct_and_flags_map_to_it():
+    """wf_fwd_cfg is {float rescale_threshold; int scheduler; int num_sms; int cluster_m;}
+    in the header; the forward feature flags fill it (cluster_mn (2, 1) -> cluster_m 0 = auto,
+    (1, 1) -> 1 = single CTAs)."""
+    import ctypes
+
+    from wan_flash import _lib, features
+    from wan_flash.interface import _fwd_cfg
+
+    assert ctypes.sizeof(_lib.FwdCfg) == 16
+    assert [f[0] for f in _lib.FwdCfg._fields_] == ["rescale_threshold", "scheduler", "num_sms", "cluster_m"]
+    cfg = _fwd_cfg(features.get())
+    assert (cfg.rescale_threshold, cfg.scheduler, cfg.num_sms, cfg.cluster_m) == (8.0, 0, 0, 0)
+    try:
+        features.set_overrides(cluster_mn=(1, 1), scheduler="persistent", num_sms=100, rescale_skip_threshold=0.0)
+        cfg = _fwd_cfg(features.get())
+        assert (cfg.rescale_threshold, cfg.scheduler, cfg.num_sms, cfg.cluster_m) == (0.0, 2, 100, 1)
+        features.set_overrides(cluster_mn=(2, 1), scheduler="single")
+        assert (_fwd_cfg(features.get()).scheduler, _fwd_cfg(features.get()).cluster_m) == (1, 0)
+    finally:
+        features.reset()
+
+
 def test_bwd_cfg_matches_c_struct_and_plan_carries_cluster_n():
     """wf_bwd_cfg is {int nsplit; int cluster_n; int deterministic; int pdl_off; int* sem;} in the header."""
     import ctypes
